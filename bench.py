@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the reused-KV hot path.
+
+Workload ("llama3-8b-8k-prompt"): one 8192-token prompt made of 16 reused
+512-token chunks placed at shuffled positions, Llama-3-8B KV shape (32
+layers, 8 KV heads x 128, bf16, block size 16, RoPE theta 5e5). One step =
+the fused store-staging -> re-rotated paged-KV load of every chunk and layer
+(flexible PIC: rotate from the saved to the new position) + top-15%
+recompute selection per layer on lognormal deviation scores (2% x20), with
+the index list and slot mapping as output.
+
+  value : reused-KV GB/s over all ranks, inputs resident in HBM. Algorithmic
+          bytes = 4 * H * D * 2 B per token per layer (K,V read from staging
+          and written to the paged cache) = 8 KiB; 2.147 GB per prompt.
+  e2e   : the same step through the public API from pinned host buffers:
+          store shm -> staging H2D (batched_memcpy_h2d), scores H2D, the
+          fused load, the selection, D2H of index list + slots.
+Multi-GPU (torchrun): requests shard data-parallel, no collective on the
+data path; each rank loads its own prompt ("scaling": "weak").
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "reused-KV GB/s per GPU (fraction of HBM peak); µs per 8K-token prompt, 1/2/4/8 GPU"
+CFG = dict(layers=32, kv_heads=8, head_dim=128, block_size=16, tokens=8192, chunk=512, theta=5e5,
+           ratio=0.15, max_pos=8192)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def algorithmic_bytes(tokens, layers, heads, dim):
+    return tokens * layers * 4 * heads * dim * 2
+
+
+def rope_table(max_pos, rot_dim, base, dtype):
+    # vLLM RotaryEmbedding._compute_cos_sin_cache (fp32 on CPU), cast to the model dtype
+    inv = 1.0 / (base ** (torch.arange(0, rot_dim, 2, dtype=torch.float) / rot_dim))
+    t = torch.arange(max_pos, dtype=torch.float)
+    f = torch.einsum("i,j -> ij", t, inv)
+    return torch.cat((f.cos(), f.sin()), dim=-1).to(dtype)
+
+
+class Workload:
+    """Synthetic config-2 inputs, seeded per rank."""
+
+    def __init__(self, device, seed=0):
+        from daric_b200.reuse import ReusedKVLoader, layer_block_bytes
+        from daric_b200.topo import CacheTopo
+        c = CFG
+        self.device = device
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        L, H, D, bs, T, C = c["layers"], c["kv_heads"], c["head_dim"], c["block_size"], c["tokens"], c["chunk"]
+        M = T // C
+        pages_per_chunk = C // bs
+        nb = T // bs + 64                      # + null block 0 and free blocks
+        self.names = [f"model.layers.{i}.self_attn.attn" for i in range(L)]
+        self.kv = {n: torch.zeros((2, nb, bs, H, D), dtype=torch.bfloat16, device=device) for n in self.names}
+        perm = torch.randperm(nb - 1, generator=g)[: T // bs] + 1
+        self.chunk_blocks = [perm[m * pages_per_chunk:(m + 1) * pages_per_chunk].tolist() for m in range(M)]
+        self.block_table = perm.to(torch.int32).to(device)
+        # chunk m is placed at m*C; it was saved at a shuffled slot
+        order = torch.randperm(M, generator=g).tolist()
+        self.new_pos = [m * C for m in range(M)]
+        self.old_pos = [order[m] * C for m in range(M)]
+        self.chunk_len = [C] * M
+        self.table = rope_table(c["max_pos"], D, c["theta"], torch.bfloat16).to(device)
+        topo = CacheTopo.single_group(self.names, bs, layer_block_bytes(self.kv[self.names[0]], False), False)
+        total = M * L * 2 * pages_per_chunk * bs * H * D * 2
+        self.staging = torch.empty(total, dtype=torch.uint8, device=device)
+        gd = torch.Generator(device=device).manual_seed(seed + 1)
+        vals = self.staging.view(torch.bfloat16).view(M, L, 2, pages_per_chunk, bs, H, D)
+        for m in range(M):  # K,V ~ N(0,1); 4 K channels per head x8
+            x = torch.randn((L, 2, pages_per_chunk, bs, H, D), generator=gd, device=device)
+            ch = torch.randperm(D, generator=g)[:4].to(device)
+            x[:, 0, ..., ch] *= 8.0
+            vals[m].copy_(x.to(torch.bfloat16))
+        del x
+        self.loader = ReusedKVLoader(self.kv, topo, self.staging,
+                                     {n: (self.table, D, True) for n in self.names})
+        self.plan = self.loader.plan([(b,) for b in self.chunk_blocks])
+        assert self.plan.total_bytes == total
+        sc = torch.distributions.LogNormal(0.0, 1.0).sample((L, T))
+        spikes = torch.rand(L, T, generator=g) < 0.02
+        self.scores_host = torch.where(spikes, sc * 20, sc).float().contiguous()
+        self.scores = self.scores_host.to(device)
+        self.sel = None
+        self.bytes = algorithmic_bytes(T, L, H, D)
+        self.tokens = T
+
+    def load(self, stream=0):
+        self.loader.load(self.plan, mode="flexible", pos_a=self.old_pos, pos_b=self.new_pos,
+                         chunk_len=self.chunk_len, stream=stream)
+
+    def select(self, scores=None):
+        from daric_b200.select import score_select
+        self.sel = score_select(scores if scores is not None else self.scores, self.block_table,
+                                CFG["block_size"], ratio=CFG["ratio"], out=self.sel)
+        return self.sel
+
+    def step(self):
+        self.load()
+        return self.select()
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            p = [x.strip() for x in l.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline_run(wl_cpu, min_seconds=3.0, max_reps=50):
+    from oracle.torch_cpu import reused_kv_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    args = wl_cpu
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        reused_kv_step(*args)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= max_reps:
+            break
+    return reps, el
+
+
+def make_cpu_workload(wl, chunks=None):
+    """The GPU workload copied to host tensors for the CPU path."""
+    M = len(wl.chunk_blocks) if chunks is None else chunks
+    L = CFG["layers"]
+    per_chunk = wl.staging.numel() // len(wl.chunk_blocks)
+    stg = wl.staging[: M * per_chunk].cpu()
+    kv = [torch.zeros_like(wl.kv[n], device="cpu") for n in wl.names]
+    blocks = [torch.tensor(b, dtype=torch.int64) for b in wl.chunk_blocks[:M]]
+    k = int(np.floor(CFG["ratio"] * CFG["chunk"] * M + 1e-9))
+    sc = wl.scores_host[:, : CFG["chunk"] * M].contiguous()
+    bt = wl.block_table.cpu()
+    return (kv, stg, blocks, wl.chunk_len[:M], wl.old_pos[:M], wl.new_pos[:M], wl.table.cpu(), sc, k, bt,
+            CFG["block_size"]), algorithmic_bytes(CFG["chunk"] * M, L, CFG["kv_heads"], CFG["head_dim"])
+
+
+def run_reference(args):
+    """--impl reference: the reference's math on the host cores (the
+    reference has no CPU implementation of this path; oracle/torch_cpu.py
+    restates it on torch CPU ops with every host thread)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT))
+    from oracle.torch_cpu import reused_kv_step
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    L, H, D, bs, C = CFG["layers"], CFG["kv_heads"], CFG["head_dim"], CFG["block_size"], CFG["chunk"]
+    pages = C // bs
+    # one step = one reused chunk x all layers (a bounded sample of the prompt)
+    stg = torch.randn(L * 2 * pages * bs * H * D, generator=g).to(torch.bfloat16).view(torch.uint8)
+    nb = CFG["tokens"] // bs + 64
+    kv = [torch.zeros((2, nb, bs, H, D), dtype=torch.bfloat16) for _ in range(L)]
+    blocks = [torch.randperm(nb - 1, generator=g)[:pages] + 1]
+    table = rope_table(CFG["max_pos"], D, CFG["theta"], torch.bfloat16)
+    sc = torch.distributions.LogNormal(0.0, 1.0).sample((L, C))
+    k = int(np.floor(CFG["ratio"] * C + 1e-9))
+    bt = blocks[0].to(torch.int32)
+    step = (kv, stg, blocks, [C], [1536], [512], table, sc, k, bt, bs)
+    for _ in range(args.warmup):
+        reused_kv_step(*step)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reused_kv_step(*step)
+    el = time.perf_counter() - t0
+    nbytes = algorithmic_bytes(C, L, H, D)
+    val = nbytes * args.steps / el / 1e9
+    sample = f"1 reused 512-token chunk x {L} layers per step (1/16 of the 8K prompt), torch CPU"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "llama3-8b-8k-prompt", "sample": "1 chunk x 32 layers per step",
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from daric_b200 import _lib
+    wl = Workload(dev, seed=rank)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            wl.load()
+            ev[i][1].record(stream)
+            wl.select()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    kern_ms = [a.elapsed_time(b) for a, b in ev]
+    t = torch.tensor([ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    errors = _lib.device_errors(local)
+
+    # ---- e2e: public API from pinned host buffers
+    from daric_b200.cache_ops import batched_memcpy_h2d
+    host_shm = torch.empty(wl.staging.numel(), dtype=torch.uint8).pin_memory()
+    host_shm.copy_(wl.staging.cpu())
+    host_scores = wl.scores_host.pin_memory()
+    sel = wl.select()
+    out_idx = torch.empty(sel.idx.shape, dtype=sel.idx.dtype).pin_memory()
+    out_slot = torch.empty(sel.slot.shape, dtype=sel.slot.dtype).pin_memory()
+    out_cnt = torch.empty(sel.count.shape, dtype=sel.count.dtype).pin_memory()
+    chunk_off = wl.plan.chunk_offsets.tolist()
+    chunk_size = wl.plan.chunk_sizes.tolist()
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        batched_memcpy_h2d(host_shm, wl.staging, chunk_off, chunk_off, chunk_size)
+        wl.scores.copy_(host_scores, non_blocking=True)
+        wl.load()
+        s = wl.select()
+        out_idx.copy_(s.idx, non_blocking=True)
+        out_slot.copy_(s.slot, non_blocking=True)
+        out_cnt.copy_(s.count, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms_max = float(t.item())
+    h2d = wl.staging.numel() + wl.scores_host.numel() * 4
+    d2h = out_idx.numel() * 4 + out_slot.numel() * 8 + out_cnt.numel() * 4
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        kern_avg_ms = sum(kern_ms) / len(kern_ms)
+        achieved = wl.bytes / (kern_avg_ms * 1e-3) / 1e9
+        traffic = None
+        tp = ROOT / "profiles" / "traffic.json"
+        if tp.exists():
+            traffic = json.loads(tp.read_text()).get("rerotate_scatter_kernel_bytes_per_launch")
+        value = world * wl.bytes * args.steps / (ms_max * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "llama3-8b-8k-prompt", "layers": CFG["layers"], "kv_heads": CFG["kv_heads"],
+                       "head_dim": CFG["head_dim"], "block_size": CFG["block_size"], "tokens": CFG["tokens"],
+                       "chunks": CFG["tokens"] // CFG["chunk"], "rope": "flexible", "theta": CFG["theta"],
+                       "select": "top15%/layer", "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (1 GiB staging + 1.2 GiB paged cache per GPU), no flush"},
+            "us_per_prompt": round(ms_max / args.steps * 1e3, 2),
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": "rotate_scatter_kernel", "peak_kind": peak_kind,
+                         "kernel_us": round(kern_avg_ms * 1e3, 2),
+                         "algorithmic_bytes_per_launch": wl.bytes},
+            "e2e": {"value": round(world * wl.bytes * e2e_steps / (e2e_ms_max * 1e-3) / 1e9, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms_max / e2e_steps, 4)},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+            "device_errors": errors,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            sys.path.insert(0, str(ROOT))
+            cw, cbytes = make_cpu_workload(wl, chunks=args.cpu_chunks)
+            reps, el = cpu_baseline_run(cw)
+            line["cpu_baseline"] = {
+                "value": round(cbytes * reps / el / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+                "kind": "port",
+                "sample": f"{args.cpu_chunks} of 16 chunks x 32 layers per pass, {reps} passes in {el:.1f}s "
+                          "(torch CPU restatement: scatter + flexible re-rotation + top-k)"}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-chunks", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

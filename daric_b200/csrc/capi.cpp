@@ -1,0 +1,901 @@
+// Host side of the C ABI declared in include/daric_b200.h.
+//
+// Responsibilities: argument validation with the reference's rules
+// (csrc/cache_ops/helpers.cu:94-174, copier.cpp:32-39, kernels.cu:151-161),
+// building the per-call device descriptors (layers, jobs, chunks) and
+// uploading them through a pinned ring, and launching the kernels on the
+// caller's stream. Nothing here blocks the host except a ring slot whose
+// previous use (16 calls earlier on the same device) is still running.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "internal.h"
+
+using namespace daric;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    g_last_error.clear();
+    return DARIC_OK;
+  } catch (const Error& e) {
+    g_last_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return DARIC_ERR_STATE;
+  }
+}
+
+std::string fmt_vec(const std::vector<int64_t>& v) {
+  std::ostringstream ss;
+  ss << "[";
+  for (size_t i = 0; i < v.size(); ++i) ss << (i ? ", " : "") << v[i];
+  ss << "]";
+  return ss.str();
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    DARIC_CUDA(cudaGetDevice(&prev));
+    if (prev != dev) DARIC_CUDA(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != prev && prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// ------------------------------------------------------ per-device state --
+constexpr int kRingSlots = 16;
+
+struct RingSlot {
+  std::mutex mu;
+  uint8_t* host = nullptr;
+  uint8_t* dev = nullptr;
+  size_t cap = 0;
+  cudaEvent_t done = nullptr;
+  bool pending = false;
+};
+
+struct DeviceCtx {
+  int device = -1;
+  int sm_count = 0;
+  int* err_word = nullptr;
+  std::mutex mu;
+  unsigned next = 0;
+  RingSlot slots[kRingSlots];
+};
+
+std::mutex g_ctx_mu;
+std::map<int, std::unique_ptr<DeviceCtx>> g_ctx;
+
+DeviceCtx& device_ctx(int device) {
+  std::lock_guard<std::mutex> g(g_ctx_mu);
+  auto it = g_ctx.find(device);
+  if (it != g_ctx.end()) return *it->second;
+  auto c = std::make_unique<DeviceCtx>();
+  c->device = device;
+  DARIC_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
+  DeviceGuard dg(device);
+  DARIC_CUDA(cudaMalloc(&c->err_word, sizeof(int)));
+  DARIC_CUDA(cudaMemset(c->err_word, 0, sizeof(int)));
+  for (auto& s : c->slots) DARIC_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+  auto& ref = *c;
+  g_ctx[device] = std::move(c);
+  return ref;
+}
+
+// One descriptor upload: a ring slot held for the duration of the call.
+class Upload {
+ public:
+  Upload(DeviceCtx& c, size_t bytes) {
+    {
+      std::lock_guard<std::mutex> g(c.mu);
+      slot_ = &c.slots[c.next++ % kRingSlots];
+    }
+    lock_ = std::unique_lock<std::mutex>(slot_->mu);
+    if (slot_->pending) {
+      DARIC_CUDA(cudaEventSynchronize(slot_->done));
+      slot_->pending = false;
+    }
+    if (slot_->cap < bytes) {
+      size_t cap = std::max<size_t>(bytes, 64 * 1024);
+      cap = std::max(cap, slot_->cap * 2);
+      if (slot_->host) DARIC_CUDA(cudaFreeHost(slot_->host));
+      if (slot_->dev) DARIC_CUDA(cudaFree(slot_->dev));
+      slot_->host = nullptr;
+      slot_->dev = nullptr;
+      slot_->cap = 0;
+      DARIC_CUDA(cudaHostAlloc((void**)&slot_->host, cap, cudaHostAllocDefault));
+      DARIC_CUDA(cudaMalloc((void**)&slot_->dev, cap));
+      slot_->cap = cap;
+    }
+  }
+  uint8_t* host() { return slot_->host; }
+  uint8_t* dev() { return slot_->dev; }
+  void send(size_t bytes, cudaStream_t s) {
+    if (bytes) DARIC_CUDA(cudaMemcpyAsync(slot_->dev, slot_->host, bytes, cudaMemcpyHostToDevice, s));
+  }
+  void finish(cudaStream_t s) {
+    DARIC_CUDA(cudaEventRecord(slot_->done, s));
+    slot_->pending = true;
+  }
+
+ private:
+  RingSlot* slot_ = nullptr;
+  std::unique_lock<std::mutex> lock_;
+};
+
+// Lays out [section 0 | section 1 | ...] with 16-byte aligned sections.
+struct Blob {
+  size_t size = 0;
+  size_t add(size_t bytes) {
+    size_t off = (size + 15) & ~size_t(15);
+    size = off + bytes;
+    return off;
+  }
+};
+
+// ----------------------------------------------------------- layers -----
+struct LayerHost {
+  std::string name;
+  uint8_t* data = nullptr;
+  int device = 0;
+  std::vector<int64_t> sizes, strides;
+  int64_t es = 1;
+  bool page_first = false;
+  int num_pages = 0, prefix_size = 0;
+  int64_t page_stride = 0, suffix = 0, prefix_stride = 0;
+  // rotation
+  bool has_rot = false;
+  int kv_dtype = -1, tab_dtype = -1, neox = 1;
+  LayerDev dev{};  // rotation part filled by register_rotary
+};
+
+int64_t checked_mul(int64_t a, int64_t b, const char* what) {
+  DARIC_CHECK(a >= 0 && b >= 0, std::string(what) + " must be non-negative");
+  DARIC_CHECK(a == 0 || b <= INT64_MAX / a, std::string(what) + " exceeds int64 range");
+  return a * b;
+}
+
+// Element span of dims [first, ndim) that must be dense in memory
+// (helpers.cu:22-64): non-singleton dims sorted by stride must have strides
+// 1, s0, s0*s1, ... .
+int64_t dense_span(const LayerHost& t, int first) {
+  struct D { int dim; int64_t size, stride; };
+  std::vector<D> dims;
+  for (int d = first; d < (int)t.sizes.size(); ++d) {
+    DARIC_CHECK(t.sizes[d] > 0, "KV cache copy dimensions must be non-empty | shape=" +
+                                    fmt_vec(t.sizes) + " | stride=" + fmt_vec(t.strides) +
+                                    " | failed_dim=" + std::to_string(d));
+    if (t.sizes[d] == 1) continue;
+    DARIC_CHECK(t.strides[d] > 0,
+                "KV cache non-singleton dimensions must have positive strides | shape=" +
+                    fmt_vec(t.sizes) + " | stride=" + fmt_vec(t.strides) +
+                    " | failed_dim=" + std::to_string(d));
+    dims.push_back({d, t.sizes[d], t.strides[d]});
+  }
+  std::stable_sort(dims.begin(), dims.end(), [](const D& a, const D& b) { return a.stride < b.stride; });
+  int64_t expect = 1;
+  for (const auto& d : dims) {
+    DARIC_CHECK(d.stride == expect,
+                "KV cache copy dimensions must form a dense physical span | shape=" +
+                    fmt_vec(t.sizes) + " | stride=" + fmt_vec(t.strides) +
+                    " | failed_dim=" + std::to_string(d.dim) + " | expected_stride=" +
+                    std::to_string(expect) + " | actual_stride=" + std::to_string(d.stride) +
+                    " | relation=" + (d.stride > expect ? "hole" : "overlap"));
+    expect = checked_mul(expect, d.size, "KV cache dense span");
+  }
+  return expect;
+}
+
+// Page-copy shape of a layer (helpers.cu:94-148).
+void page_copy_shape(LayerHost& t) {
+  const int nd = (int)t.sizes.size();
+  DARIC_CHECK(nd >= 1, "KV cache tensor must have at least one dimension");
+  if (t.page_first) {
+    DARIC_CHECK(t.sizes[0] > 0, "page dimension must be non-zero");
+    DARIC_CHECK(t.sizes[0] <= INT32_MAX, "number of pages exceeds int range: " + std::to_string(t.sizes[0]));
+    t.num_pages = (int)t.sizes[0];
+    t.prefix_size = 1;
+    t.prefix_stride = 0;
+    t.page_stride = checked_mul(t.strides[0], t.es, "KV cache page stride");
+    t.suffix = checked_mul(dense_span(t, 1), t.es, "KV cache page span");
+    if (t.num_pages > 1)
+      DARIC_CHECK(t.page_stride >= t.suffix,
+                  "KV cache pages overlap | shape=" + fmt_vec(t.sizes) + " | stride=" +
+                      fmt_vec(t.strides) + " | page_stride=" + std::to_string(t.page_stride) +
+                      " | page_span=" + std::to_string(t.suffix));
+  } else {
+    DARIC_CHECK(nd >= 2, "non-page-first KV cache tensor must have at least two dimensions");
+    DARIC_CHECK(t.sizes[0] > 0, "prefix dimension must be non-zero");
+    DARIC_CHECK(t.sizes[1] > 0, "page dimension must be non-zero");
+    DARIC_CHECK(t.sizes[0] <= INT32_MAX, "prefix size exceeds int range: " + std::to_string(t.sizes[0]));
+    DARIC_CHECK(t.sizes[1] <= INT32_MAX, "number of pages exceeds int range: " + std::to_string(t.sizes[1]));
+    t.prefix_size = (int)t.sizes[0];
+    t.num_pages = (int)t.sizes[1];
+    t.prefix_stride = checked_mul(t.strides[0], t.es, "KV cache prefix stride");
+    t.page_stride = checked_mul(t.strides[1], t.es, "KV cache page stride");
+    t.suffix = checked_mul(dense_span(t, 2), t.es, "KV cache suffix span");
+    // prefix/page regions must not overlap (helpers.cu:66-90)
+    std::vector<std::pair<int64_t, int64_t>> axes;
+    if (t.prefix_size > 1) axes.emplace_back(t.prefix_stride, t.prefix_size);
+    if (t.num_pages > 1) axes.emplace_back(t.page_stride, t.num_pages);
+    std::sort(axes.begin(), axes.end());
+    int64_t span = t.suffix;
+    for (auto& [stride, size] : axes) {
+      DARIC_CHECK(stride >= span, "KV cache prefix/page regions overlap | shape=" + fmt_vec(t.sizes) +
+                                      " | stride=" + fmt_vec(t.strides) + " | region_size=" +
+                                      std::to_string(t.suffix) + " | required_stride=" +
+                                      std::to_string(span) + " | actual_stride=" + std::to_string(stride));
+      const int64_t ext = checked_mul(size - 1, stride, "KV cache outer span");
+      DARIC_CHECK(ext <= INT64_MAX - span, "KV cache outer span exceeds int64 range");
+      span += ext;
+    }
+  }
+  DARIC_CHECK(t.page_stride > 0, "page_stride must be positive");
+}
+
+int dtype_size(int dt) {
+  switch (dt) {
+    case DARIC_DTYPE_F32: return 4;
+    case DARIC_DTYPE_F16:
+    case DARIC_DTYPE_BF16: return 2;
+    case DARIC_DTYPE_FP8_E4M3: return 1;
+  }
+  throw Error(DARIC_ERR_INVALID, "unknown dtype code " + std::to_string(dt));
+}
+
+}  // namespace
+
+struct daric_copier {
+  std::unordered_map<std::string, LayerHost> layers;
+  bool has_store = false;
+  uint8_t* store = nullptr;
+  int64_t store_bytes = 0;
+  int store_device = -1;
+};
+
+namespace {
+
+LayerHost& find_layer(daric_copier* c, const char* name) {
+  DARIC_CHECK(name != nullptr, "layer name is NULL");
+  auto it = c->layers.find(name);
+  DARIC_CHECK(it != c->layers.end(), std::string("layer not registered: ") + name);
+  return it->second;
+}
+
+LayerDev base_layer_dev(const LayerHost& L) {
+  LayerDev d = L.dev;
+  d.base = L.data;
+  d.page_stride = L.page_stride;
+  d.prefix_stride = L.prefix_stride;
+  d.suffix = L.suffix;
+  d.prefix_size = L.prefix_size;
+  d.num_pages = L.num_pages;
+  d.has_rot = L.has_rot ? 1 : 0;
+  return d;
+}
+
+// Job validation common to gather/scatter (helpers.cu:150-174,
+// copier.cpp:32-39) and the byte-size check (kernels.cu:151-161).
+struct JobPlan {
+  std::vector<LayerHost*> layers;  // per job
+  std::vector<int> layer_slot;     // per job, index into uniq
+  std::vector<LayerHost*> uniq;
+  std::vector<int64_t> n_sel;
+  int64_t total_units = 0;
+  int device = -1;
+  bool vec16 = true;
+};
+
+JobPlan plan_jobs(daric_copier* c, int64_t num_jobs, const char* const* names, const int64_t* offsets,
+                  const int64_t* byte_sizes, const int32_t* indices_flat, int64_t indices_numel,
+                  int indices_device, const int64_t* indices_offsets) {
+  DARIC_CHECK(c != nullptr, "copier is NULL");
+  DARIC_CHECK(c->has_store, "store buffer not registered; call register_store() first");
+  JobPlan jp;
+  DARIC_CHECK(num_jobs >= 0, "num_jobs must be non-negative");
+  if (num_jobs == 0) return jp;
+  DARIC_CHECK(names && offsets && byte_sizes && indices_offsets, "job arrays must not be NULL");
+  DARIC_CHECK(indices_flat != nullptr || indices_numel == 0, "indices_flat is NULL");
+  DARIC_CHECK(indices_offsets[0] >= 0, "indices_offsets[0] must be non-negative");
+  DARIC_CHECK(indices_offsets[num_jobs] <= indices_numel,
+              "indices_offsets.back() exceeds indices_flat.numel()");
+  for (int64_t i = 0; i < num_jobs; ++i) {
+    DARIC_CHECK(offsets[i] >= 0, "negative store offset at job " + std::to_string(i));
+    DARIC_CHECK(byte_sizes[i] >= 0, "negative byte size at job " + std::to_string(i));
+    DARIC_CHECK(indices_offsets[i] >= 0, "negative indices offset at job " + std::to_string(i));
+    DARIC_CHECK(indices_offsets[i] <= indices_offsets[i + 1],
+                "indices_offsets must be non-decreasing at job " + std::to_string(i));
+    DARIC_CHECK(offsets[i] <= c->store_bytes, "store offset out of range at job " + std::to_string(i));
+    DARIC_CHECK(byte_sizes[i] <= c->store_bytes - offsets[i],
+                "store range out of bounds at job " + std::to_string(i));
+  }
+  std::unordered_map<LayerHost*, int> slot_of;
+  jp.layers.resize(num_jobs);
+  jp.layer_slot.resize(num_jobs);
+  jp.n_sel.resize(num_jobs);
+  for (int64_t i = 0; i < num_jobs; ++i) {
+    LayerHost& L = find_layer(c, names[i]);
+    if (i == 0) jp.device = L.device;
+    DARIC_CHECK(L.device == jp.device,
+                "all layers must be on the same device; job " + std::to_string(i));
+    jp.layers[i] = &L;
+    auto it = slot_of.find(&L);
+    if (it == slot_of.end()) {
+      it = slot_of.emplace(&L, (int)jp.uniq.size()).first;
+      jp.uniq.push_back(&L);
+    }
+    jp.layer_slot[i] = it->second;
+    const int64_t ns = indices_offsets[i + 1] - indices_offsets[i];
+    DARIC_CHECK(ns <= INT32_MAX, "too many pages in job " + std::to_string(i));
+    jp.n_sel[i] = ns;
+    const int64_t expect = (int64_t)L.prefix_size * ns * L.suffix;
+    if (byte_sizes[i] != expect) {
+      std::ostringstream ss;
+      ss << "byte_size mismatch at job " << i << " | C++ expected bytes: " << expect
+         << " | Python passed bytes: " << byte_sizes[i] << " | Tensor shape: " << fmt_vec(L.sizes)
+         << " | Tensor strides: " << fmt_vec(L.strides);
+      throw Error(DARIC_ERR_INVALID, ss.str());
+    }
+    if (L.suffix % 16 || L.page_stride % 16 || L.prefix_stride % 16 || expect % 16 || offsets[i] % 16 ||
+        ((uintptr_t)L.data % 16))
+      jp.vec16 = false;
+    jp.total_units += ns;
+  }
+  if ((uintptr_t)c->store % 16) jp.vec16 = false;
+  DARIC_CHECK(indices_device == jp.device, "indices_flat must be on the same device as kvcache");
+  DARIC_CHECK(c->store_device == jp.device, "store buffer must be on the same device as kvcache");
+  return jp;
+}
+
+// Builds and launches page jobs. mode/metas only for the rotating scatter.
+void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t>& job_index,
+                   const int64_t* offsets, const int32_t* indices_flat, int64_t indices_numel,
+                   const int64_t* indices_offsets, bool gather, bool rotate, int mode,
+                   const int64_t* job_meta, const std::vector<MetaDev>& metas, float* scores,
+                   int64_t score_ld, const int64_t* job_score_row, RotKey key, cudaStream_t stream) {
+  DeviceCtx& dc = device_ctx(jp.device);
+  // Layer table restricted to this launch's layers.
+  std::vector<int> slot_map(jp.uniq.size(), -1);
+  std::vector<LayerDev> layers;
+  std::vector<JobDev> jobs;
+  jobs.reserve(job_index.size());
+  int64_t units = 0;
+  for (int64_t i : job_index) {
+    const int us = jp.layer_slot[i];
+    if (slot_map[us] < 0) {
+      slot_map[us] = (int)layers.size();
+      layers.push_back(base_layer_dev(*jp.uniq[us]));
+    }
+    if (jp.n_sel[i] == 0) continue;
+    JobDev j{};
+    j.stg_off = offsets[i];
+    j.idx_off = indices_offsets[i];
+    j.unit_begin = units;
+    j.n_sel = (int32_t)jp.n_sel[i];
+    j.layer = slot_map[us];
+    j.meta = rotate ? (int32_t)job_meta[i] : -1;
+    j.score_row = (rotate && scores) ? (int32_t)job_score_row[i] : -1;
+    jobs.push_back(j);
+    units += jp.n_sel[i];
+  }
+  if (units == 0) return;
+  DeviceGuard dg(jp.device);
+  Blob b;
+  const size_t o_layers = b.add(layers.size() * sizeof(LayerDev));
+  const size_t o_jobs = b.add(jobs.size() * sizeof(JobDev));
+  const size_t o_metas = b.add(metas.size() * sizeof(MetaDev));
+  Upload up(dc, b.size);
+  std::memcpy(up.host() + o_layers, layers.data(), layers.size() * sizeof(LayerDev));
+  std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
+  if (!metas.empty()) std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
+  up.send(b.size, stream);
+  PageLaunch p{};
+  p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_layers);
+  p.jobs = reinterpret_cast<const JobDev*>(up.dev() + o_jobs);
+  p.metas = reinterpret_cast<const MetaDev*>(up.dev() + o_metas);
+  p.store = c->store;
+  p.store_mut = c->store;
+  p.indices = indices_flat;
+  p.indices_numel = indices_numel;
+  p.num_jobs = (int64_t)jobs.size();
+  p.total_units = units;
+  p.mode = mode;
+  p.scores = scores;
+  p.score_ld = score_ld;
+  p.err = dc.err_word;
+  p.smem_bytes = 0;
+  for (const auto& l : layers) p.smem_bytes = std::max(p.smem_bytes, rotate_smem_bytes(l.page_size, l.half_rot));
+  if (rotate) launch_rotate_scatter(p, key, dc.sm_count, stream);
+  else launch_plain_pages(p, gather, jp.vec16, dc.sm_count, stream);
+  up.finish(stream);
+}
+
+void do_copy(daric_copier* c, bool gather, int64_t num_jobs, const char* const* names,
+             const int64_t* offsets, const int64_t* byte_sizes, const int32_t* indices_flat,
+             int64_t indices_numel, int indices_device, const int64_t* indices_offsets, void* stream) {
+  JobPlan jp = plan_jobs(c, num_jobs, names, offsets, byte_sizes, indices_flat, indices_numel,
+                         indices_device, indices_offsets);
+  if (num_jobs == 0 || jp.total_units == 0) return;
+  std::vector<int64_t> all(num_jobs);
+  for (int64_t i = 0; i < num_jobs; ++i) all[i] = i;
+  run_page_jobs(c, jp, all, offsets, indices_flat, indices_numel, indices_offsets, gather, false,
+                DARIC_ROPE_NONE, nullptr, {}, nullptr, 0, nullptr, RotKey{}, (cudaStream_t)stream);
+}
+
+// Rotation geometry of a registered layer (adapter.py:311-368 stride rules).
+void resolve_rotary(LayerHost& L, int kv_dtype, const void* table, int tab_dtype, int64_t max_pos,
+                    int64_t rot_dim, int neox) {
+  const int kv_es = dtype_size(kv_dtype);
+  DARIC_CHECK(kv_es == L.es, "kv_dtype size does not match the registered element size");
+  const int tab_es = dtype_size(tab_dtype);
+  DARIC_CHECK(tab_dtype != DARIC_DTYPE_FP8_E4M3, "fp8 rotary tables are not supported");
+  DARIC_CHECK(table != nullptr, "cos_sin_cache is NULL");
+  DARIC_CHECK(max_pos > 0, "cos_sin_cache must have at least one row");
+  const auto& s = L.sizes;
+  const auto& st = L.strides;
+  const int nd = (int)s.size();
+  int64_t nrows = 0, row_elems = 0, head_dim = 0, tok_div = 1, page_size = 0;
+  int k_prefix = 0;
+  if (nd == 5) {
+    // page-first (nb, 2, bs, H, D) or (2, nb, bs, H, D): K rows (bs, H) dense.
+    page_size = s[2];
+    const int64_t H = s[3], D = s[4];
+    DARIC_CHECK(st[4] == 1 && (H == 1 || st[3] == D) && (page_size == 1 || st[2] == H * D),
+                "rerotate: 5-D KV cache needs dense (block_size, heads, head_dim) K rows");
+    nrows = page_size * H;
+    row_elems = D;
+    head_dim = D;
+    tok_div = H;
+    k_prefix = 0;
+  } else if (nd == 4) {
+    DARIC_CHECK(L.page_first, "Invalid 4D KV cache for rerotate: page_first must be true");
+    const int64_t H = s[1], packed = s[3];
+    page_size = s[2];
+    DARIC_CHECK(packed > 0 && packed % 2 == 0,
+                "Invalid 4D KV cache for rerotate: packed content dimension must be positive and even");
+    DARIC_CHECK(st[3] == 1, "Invalid 4D KV cache for rerotate: packed content feature stride must equal 1");
+    DARIC_CHECK((page_size == 1 || st[2] == packed) && (H == 1 || st[1] == page_size * packed),
+                "rerotate: 4-D KV cache needs dense (heads, block_size, packed) rows");
+    head_dim = packed / 2;
+    nrows = H * page_size;
+    row_elems = packed;
+    tok_div = 1;
+  } else if (nd == 3) {
+    DARIC_CHECK(L.page_first, "rerotate: 3-D KV cache must be registered page_first");
+    page_size = s[1];
+    DARIC_CHECK(st[2] == 1 && (page_size == 1 || st[1] == s[2]), "rerotate: 3-D KV cache rows must be dense");
+    nrows = page_size;
+    row_elems = s[2];
+    head_dim = s[2];
+    tok_div = 1;
+  } else {
+    throw Error(DARIC_ERR_INVALID, "Unsupported KV cache rank for rerotate: " + std::to_string(nd));
+  }
+  DARIC_CHECK(rot_dim > 0 && rot_dim % 2 == 0 && rot_dim <= head_dim,
+              "rotary_dim must be positive, even, and no greater than the K head dimension");
+  DARIC_CHECK(page_size >= 1 && page_size <= 1024, "rerotate: block size must be in [1, 1024]");
+  DARIC_CHECK(rotate_smem_bytes((int)page_size, (int)(rot_dim / 2)) <= 200 * 1024,
+              "rerotate: block_size * rotary_dim too large for the shared-memory factor table");
+  const int64_t half = rot_dim / 2;
+  const int64_t row_bytes = row_elems * kv_es;
+  DARIC_CHECK(row_bytes % 16 == 0, "rerotate: K row bytes must be a multiple of 16");
+  if (neox) DARIC_CHECK((half * kv_es) % 16 == 0, "rerotate: rotary_dim/2 * element size must be a multiple of 16");
+  else DARIC_CHECK((rot_dim * kv_es) % 16 == 0, "rerotate: rotary_dim * element size must be a multiple of 16");
+  DARIC_CHECK((half * tab_es) % 16 == 0 && ((uintptr_t)table % 16) == 0,
+              "rerotate: cos_sin_cache must be 16-byte aligned with 16-byte aligned halves");
+  DARIC_CHECK(nrows * row_bytes <= L.suffix, "rerotate: K rows exceed the page region");
+  DARIC_CHECK(((uintptr_t)L.data % 16) == 0 && L.page_stride % 16 == 0 && L.prefix_stride % 16 == 0 &&
+                  L.suffix % 16 == 0,
+              "rerotate: KV layer must be 16-byte aligned");
+  DARIC_CHECK(nrows * (row_bytes / 16) < INT32_MAX, "rerotate: page too large");
+  LayerDev& d = L.dev;
+  d.k_prefix = k_prefix;
+  d.nrows = (int32_t)nrows;
+  d.row_bytes = (int32_t)row_bytes;
+  d.row_vecs = (int32_t)(row_bytes / 16);
+  d.rot_vecs = (int32_t)(rot_dim * kv_es / 16);
+  d.pair_vecs = neox ? d.rot_vecs / 2 : d.rot_vecs;
+  d.page_size = (int32_t)page_size;
+  d.pair_div = make_fastdiv((uint32_t)d.pair_vecs);
+  d.tok_div = make_fastdiv((uint32_t)tok_div);
+  d.tok_mod = make_fastdiv((uint32_t)page_size);
+  d.tail_vecs = d.row_vecs - d.rot_vecs;
+  d.tail_div = make_fastdiv((uint32_t)(d.tail_vecs > 0 ? d.tail_vecs : 1));
+  d.half_rot = (int32_t)half;
+  d.table = (const uint8_t*)table;
+  d.table_row = rot_dim * tab_es;
+  d.max_pos = max_pos;
+  L.has_rot = true;
+  L.kv_dtype = kv_dtype;
+  L.tab_dtype = tab_dtype;
+  L.neox = neox ? 1 : 0;
+}
+
+}  // namespace
+
+// ===================================================================== C ==
+extern "C" {
+
+const char* daric_last_error(void) { return g_last_error.c_str(); }
+
+int daric_version(void) { return 100; }
+
+int daric_device_sm_count(int device, int* out) {
+  return guarded([&] {
+    DARIC_CHECK(out, "out is NULL");
+    *out = device_ctx(device).sm_count;
+  });
+}
+
+int daric_device_errors(int device, int* out_bits) {
+  return guarded([&] {
+    DARIC_CHECK(out_bits, "out_bits is NULL");
+    DeviceCtx& dc = device_ctx(device);
+    DeviceGuard dg(device);
+    int v = 0;
+    DARIC_CUDA(cudaDeviceSynchronize());
+    DARIC_CUDA(cudaMemcpy(&v, dc.err_word, sizeof(int), cudaMemcpyDeviceToHost));
+    DARIC_CUDA(cudaMemset(dc.err_word, 0, sizeof(int)));
+    *out_bits = v;
+  });
+}
+
+int daric_copier_create(daric_copier** out) {
+  return guarded([&] {
+    DARIC_CHECK(out, "out is NULL");
+    *out = new daric_copier();
+  });
+}
+
+void daric_copier_destroy(daric_copier* c) { delete c; }
+
+int daric_copier_register_layer(daric_copier* c, const char* name, void* data, int device, int ndim,
+                                const int64_t* sizes, const int64_t* strides, int64_t element_size,
+                                int is_page_first) {
+  return guarded([&] {
+    DARIC_CHECK(c && name, "copier/name is NULL");
+    DARIC_CHECK(device >= 0, std::string("kvcache tensor must be on GPU: ") + name);
+    DARIC_CHECK(ndim >= 1 && sizes && strides, "KV cache tensor must have at least one dimension");
+    DARIC_CHECK(element_size > 0, "element_size must be positive");
+    LayerHost L;
+    L.name = name;
+    L.data = (uint8_t*)data;
+    L.device = device;
+    L.sizes.assign(sizes, sizes + ndim);
+    L.strides.assign(strides, strides + ndim);
+    L.es = element_size;
+    L.page_first = is_page_first != 0;
+    page_copy_shape(L);
+    c->layers.insert_or_assign(std::string(name), std::move(L));
+  });
+}
+
+int daric_copier_register_store(daric_copier* c, void* data, int64_t nbytes, int device) {
+  return guarded([&] {
+    DARIC_CHECK(c, "copier is NULL");
+    DARIC_CHECK(device >= 0, "staging buffer must be on CUDA");
+    DARIC_CHECK(nbytes >= 0 && (data || nbytes == 0), "store buffer must be a valid device range");
+    c->store = (uint8_t*)data;
+    c->store_bytes = nbytes;
+    c->store_device = device;
+    c->has_store = true;
+  });
+}
+
+int daric_copier_register_rotary(daric_copier* c, const char* layer_name, int kv_dtype,
+                                 const void* table, int tab_dtype, int64_t max_pos, int64_t rot_dim,
+                                 int is_neox) {
+  return guarded([&] {
+    DARIC_CHECK(c, "copier is NULL");
+    LayerHost& L = find_layer(c, layer_name);
+    resolve_rotary(L, kv_dtype, table, tab_dtype, max_pos, rot_dim, is_neox);
+  });
+}
+
+int daric_copier_gather_pages(daric_copier* c, int64_t num_jobs, const char* const* names,
+                              const int64_t* offsets, const int64_t* byte_sizes,
+                              const int32_t* indices_flat, int64_t indices_numel, int indices_device,
+                              const int64_t* indices_offsets, void* stream) {
+  return guarded([&] {
+    do_copy(c, true, num_jobs, names, offsets, byte_sizes, indices_flat, indices_numel, indices_device,
+            indices_offsets, stream);
+  });
+}
+
+int daric_copier_scatter_pages(daric_copier* c, int64_t num_jobs, const char* const* names,
+                               const int64_t* offsets, const int64_t* byte_sizes,
+                               const int32_t* indices_flat, int64_t indices_numel, int indices_device,
+                               const int64_t* indices_offsets, void* stream) {
+  return guarded([&] {
+    do_copy(c, false, num_jobs, names, offsets, byte_sizes, indices_flat, indices_numel, indices_device,
+            indices_offsets, stream);
+  });
+}
+
+int daric_copier_rerotate_scatter_pages(
+    daric_copier* c, int64_t num_jobs, const char* const* names, const int64_t* offsets,
+    const int64_t* byte_sizes, const int32_t* indices_flat, int64_t indices_numel, int indices_device,
+    const int64_t* indices_offsets, const int64_t* job_meta, int mode, int64_t num_metas,
+    const int64_t* meta_pos_a, const int64_t* meta_pos_b, const int64_t* meta_len, float* scores,
+    int64_t score_ld, const int64_t* job_score_row, const int64_t* meta_score_col, void* stream) {
+  return guarded([&] {
+    DARIC_CHECK(mode == DARIC_ROPE_FLEXIBLE || mode == DARIC_ROPE_DELTA || mode == DARIC_ROPE_NONE,
+                "unknown rotation mode " + std::to_string(mode));
+    JobPlan jp = plan_jobs(c, num_jobs, names, offsets, byte_sizes, indices_flat, indices_numel,
+                           indices_device, indices_offsets);
+    if (num_jobs == 0 || jp.total_units == 0) return;
+    DARIC_CHECK(num_metas >= 0 && (num_metas == 0 || (meta_pos_a && meta_len)), "chunk arrays are NULL");
+    DARIC_CHECK(mode != DARIC_ROPE_FLEXIBLE || num_metas == 0 || meta_pos_b,
+                "FLEXIBLE mode needs meta_pos_b (new positions)");
+    DARIC_CHECK(job_meta != nullptr, "job_meta is NULL");
+    if (scores) {
+      DARIC_CHECK(job_score_row && meta_score_col, "scores need job_score_row and meta_score_col");
+      DARIC_CHECK(score_ld >= 0, "score_ld must be non-negative");
+    }
+    std::vector<MetaDev> metas(num_metas);
+    for (int64_t m = 0; m < num_metas; ++m) {
+      MetaDev& d = metas[m];
+      d.pos_a = meta_pos_a[m];
+      d.pos_b = mode == DARIC_ROPE_FLEXIBLE ? meta_pos_b[m] : 0;
+      d.len = meta_len[m];
+      DARIC_CHECK(d.len >= 0, "negative chunk length at chunk " + std::to_string(m));
+      d.score_col = scores ? meta_score_col[m] : 0;
+      if (scores) DARIC_CHECK(d.score_col >= 0, "negative score column at chunk " + std::to_string(m));
+      d.rotate = (mode == DARIC_ROPE_NONE || d.len == 0 ||
+                  (mode == DARIC_ROPE_FLEXIBLE && d.pos_a == d.pos_b)) ? 0 : 1;
+    }
+    // Group jobs by kernel signature (dtype of KV, dtype of table, NeoX).
+    std::map<std::tuple<int, int, int>, std::vector<int64_t>> groups;
+    for (int64_t i = 0; i < num_jobs; ++i) {
+      const LayerHost& L = *jp.layers[i];
+      DARIC_CHECK(job_meta[i] >= 0 && job_meta[i] < num_metas,
+                  "job_meta out of range at job " + std::to_string(i));
+      DARIC_CHECK(L.has_rot || mode == DARIC_ROPE_NONE,
+                  "layer has no rotary table (register_rotary): " + L.name);
+      if (scores)
+        DARIC_CHECK(job_score_row[i] >= 0 && job_score_row[i] <= INT32_MAX,
+                    "job_score_row out of range at job " + std::to_string(i));
+      groups[{L.has_rot ? L.kv_dtype : -1, L.has_rot ? L.tab_dtype : -1, L.neox}].push_back(i);
+    }
+    for (auto& [k, idx] : groups) {
+      const bool rot = std::get<0>(k) >= 0;
+      if (rot) {
+        DARIC_CHECK(jp.vec16, "rerotate_scatter_pages needs 16-byte aligned jobs and store offsets");
+        run_page_jobs(c, jp, idx, offsets, indices_flat, indices_numel, indices_offsets, false, true,
+                      mode, job_meta, metas, scores, score_ld, job_score_row,
+                      RotKey{std::get<0>(k), std::get<1>(k), std::get<2>(k)}, (cudaStream_t)stream);
+      } else {
+        run_page_jobs(c, jp, idx, offsets, indices_flat, indices_numel, indices_offsets, false, false,
+                      DARIC_ROPE_NONE, nullptr, {}, nullptr, 0, nullptr, RotKey{}, (cudaStream_t)stream);
+      }
+    }
+  });
+}
+
+int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const char* const* names, int mode,
+                                  int64_t num_segs, const int32_t* block_table, int64_t block_table_numel,
+                                  const int64_t* seg_blk_off, const int64_t* seg_tok_start,
+                                  const int64_t* seg_tok_len, const int64_t* seg_pos_a,
+                                  const int64_t* seg_pos_b, void* stream) {
+  return guarded([&] {
+    DARIC_CHECK(c, "copier is NULL");
+    DARIC_CHECK(mode == DARIC_ROPE_FLEXIBLE || mode == DARIC_ROPE_DELTA,
+                "rerotate_inplace: mode must be FLEXIBLE or DELTA");
+    if (num_layers <= 0 || num_segs <= 0) return;
+    DARIC_CHECK(names && seg_blk_off && seg_tok_start && seg_tok_len && seg_pos_a, "segment arrays are NULL");
+    DARIC_CHECK(mode != DARIC_ROPE_FLEXIBLE || seg_pos_b, "FLEXIBLE mode needs seg_pos_b");
+    DARIC_CHECK(block_table != nullptr, "block_table is NULL");
+    std::vector<LayerHost*> layers(num_layers);
+    for (int64_t l = 0; l < num_layers; ++l) {
+      layers[l] = &find_layer(c, names[l]);
+      DARIC_CHECK(layers[l]->has_rot, "layer has no rotary table (register_rotary): " + layers[l]->name);
+    }
+    const LayerHost& L0 = *layers[0];
+    for (auto* L : layers) {
+      DARIC_CHECK(L->device == L0.device, "all layers must be on the same device");
+      DARIC_CHECK(L->kv_dtype == L0.kv_dtype && L->tab_dtype == L0.tab_dtype && L->neox == L0.neox &&
+                      L->dev.page_size == L0.dev.page_size,
+                  "rerotate_inplace: layers of one call must share dtype, table dtype, style and block size");
+    }
+    const int64_t bs = L0.dev.page_size;
+    std::vector<SegDev> segs;
+    segs.reserve(num_segs);
+    int64_t units = 0;
+    for (int64_t s = 0; s < num_segs; ++s) {
+      DARIC_CHECK(seg_tok_len[s] >= 0 && seg_tok_start[s] >= 0 && seg_blk_off[s] >= 0,
+                  "negative segment field at segment " + std::to_string(s));
+      if (seg_tok_len[s] == 0) continue;
+      SegDev d{};
+      d.blk_off = seg_blk_off[s];
+      d.tok_start = seg_tok_start[s];
+      d.tok_len = seg_tok_len[s];
+      d.pos_a = seg_pos_a[s];
+      d.pos_b = mode == DARIC_ROPE_FLEXIBLE ? seg_pos_b[s] : 0;
+      const int64_t p0 = d.tok_start / bs, p1 = (d.tok_start + d.tok_len - 1) / bs;
+      DARIC_CHECK(d.blk_off + p1 < block_table_numel,
+                  "segment " + std::to_string(s) + " reaches past the block table");
+      d.first_page = (int32_t)p0;
+      d.num_units = (int32_t)(p1 - p0 + 1);
+      d.unit_begin = units;
+      units += d.num_units;
+      segs.push_back(d);
+    }
+    if (units == 0) return;
+    DeviceCtx& dc = device_ctx(L0.device);
+    DeviceGuard dg(L0.device);
+    std::vector<LayerDev> ld(num_layers);
+    for (int64_t l = 0; l < num_layers; ++l) ld[l] = base_layer_dev(*layers[l]);
+    Blob b;
+    const size_t o_l = b.add(ld.size() * sizeof(LayerDev));
+    const size_t o_s = b.add(segs.size() * sizeof(SegDev));
+    Upload up(dc, b.size);
+    std::memcpy(up.host() + o_l, ld.data(), ld.size() * sizeof(LayerDev));
+    std::memcpy(up.host() + o_s, segs.data(), segs.size() * sizeof(SegDev));
+    up.send(b.size, (cudaStream_t)stream);
+    InplaceLaunch p{};
+    p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_l);
+    p.num_layers = num_layers;
+    p.segs = reinterpret_cast<const SegDev*>(up.dev() + o_s);
+    p.num_segs = (int64_t)segs.size();
+    p.units_per_layer = units;
+    p.block_table = block_table;
+    p.block_table_numel = block_table_numel;
+    p.mode = mode;
+    p.err = dc.err_word;
+    p.smem_bytes = 0;
+    for (const auto& l : ld) p.smem_bytes = std::max(p.smem_bytes, rotate_smem_bytes(l.page_size, l.half_rot));
+    launch_rotate_inplace(p, RotKey{L0.kv_dtype, L0.tab_dtype, L0.neox}, dc.sm_count, (cudaStream_t)stream);
+    up.finish((cudaStream_t)stream);
+  });
+}
+
+int daric_batched_memcpy_d2h(const void* staging, void* host, int64_t n, const int64_t* stg_offsets,
+                             const int64_t* host_offsets, const int64_t* sizes, int device, void* stream) {
+  return guarded([&] {
+    if (n <= 0) return;
+    DARIC_CHECK(staging && host && stg_offsets && host_offsets && sizes, "NULL argument");
+    DeviceGuard dg(device);
+    for (int64_t i = 0; i < n; ++i) {
+      DARIC_CHECK(sizes[i] >= 0 && stg_offsets[i] >= 0 && host_offsets[i] >= 0,
+                  "negative copy region at " + std::to_string(i));
+      if (sizes[i] == 0) continue;
+      DARIC_CUDA(cudaMemcpyAsync((uint8_t*)host + host_offsets[i], (const uint8_t*)staging + stg_offsets[i],
+                                 (size_t)sizes[i], cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    }
+  });
+}
+
+int daric_batched_memcpy_h2d(const void* host, void* staging, int64_t n, const int64_t* host_offsets,
+                             const int64_t* stg_offsets, const int64_t* sizes, int device, void* stream) {
+  return guarded([&] {
+    if (n <= 0) return;
+    DARIC_CHECK(staging && host && stg_offsets && host_offsets && sizes, "NULL argument");
+    DeviceGuard dg(device);
+    for (int64_t i = 0; i < n; ++i) {
+      DARIC_CHECK(sizes[i] >= 0 && stg_offsets[i] >= 0 && host_offsets[i] >= 0,
+                  "negative copy region at " + std::to_string(i));
+      if (sizes[i] == 0) continue;
+      DARIC_CUDA(cudaMemcpyAsync((uint8_t*)staging + stg_offsets[i], (const uint8_t*)host + host_offsets[i],
+                                 (size_t)sizes[i], cudaMemcpyHostToDevice, (cudaStream_t)stream));
+    }
+  });
+}
+
+int daric_score_select(const float* scores, int64_t num_layers, int64_t score_ld, int64_t num_segs,
+                       const int64_t* seg_col_off, const int64_t* seg_len, const int64_t* seg_pos0,
+                       const int64_t* seg_k, int mode, float threshold, const int32_t* block_table,
+                       int64_t block_table_numel, const int64_t* seg_blk_off, int64_t block_size,
+                       int32_t* out_idx, int64_t* out_slot, int32_t* out_count, int64_t out_ld,
+                       const int64_t* out_off, int device, void* stream) {
+  return guarded([&] {
+    DARIC_CHECK(mode == DARIC_SELECT_TOPK || mode == DARIC_SELECT_THRESHOLD,
+                "unknown selection mode " + std::to_string(mode));
+    if (num_layers <= 0 || num_segs <= 0) return;
+    DARIC_CHECK(scores && out_idx && out_slot && out_count, "NULL device pointer");
+    DARIC_CHECK(seg_col_off && seg_len && seg_pos0 && seg_blk_off && out_off, "NULL segment array");
+    DARIC_CHECK(mode != DARIC_SELECT_TOPK || seg_k, "TOPK needs seg_k");
+    DARIC_CHECK(block_size > 0, "block_size must be positive");
+    DARIC_CHECK(block_table != nullptr || block_table_numel == 0, "block_table is NULL");
+    std::vector<SelSegDev> segs(num_segs);
+    for (int64_t s = 0; s < num_segs; ++s) {
+      SelSegDev& d = segs[s];
+      d.col_off = seg_col_off[s];
+      d.len = seg_len[s];
+      d.pos0 = seg_pos0[s];
+      d.k = mode == DARIC_SELECT_TOPK ? seg_k[s] : 0;
+      d.blk_off = seg_blk_off[s];
+      d.out_off = out_off[s];
+      DARIC_CHECK(d.col_off >= 0 && d.len >= 0 && d.pos0 >= 0 && d.k >= 0 && d.blk_off >= 0 && d.out_off >= 0,
+                  "negative segment field at segment " + std::to_string(s));
+      DARIC_CHECK(d.col_off + d.len <= score_ld || num_layers == 1,
+                  "segment " + std::to_string(s) + " exceeds the score row");
+      DARIC_CHECK(d.pos0 + d.len <= INT32_MAX, "positions exceed int32");
+      const int64_t cap = mode == DARIC_SELECT_TOPK ? std::min(d.k, d.len) : d.len;
+      DARIC_CHECK(d.out_off + cap <= out_ld || num_layers == 1,
+                  "segment " + std::to_string(s) + " output exceeds out_ld");
+    }
+    DeviceCtx& dc = device_ctx(device);
+    DeviceGuard dg(device);
+    Upload up(dc, segs.size() * sizeof(SelSegDev));
+    std::memcpy(up.host(), segs.data(), segs.size() * sizeof(SelSegDev));
+    up.send(segs.size() * sizeof(SelSegDev), (cudaStream_t)stream);
+    SelectLaunch p{};
+    p.scores = scores;
+    p.num_layers = num_layers;
+    p.score_ld = score_ld;
+    p.num_segs = num_segs;
+    p.segs = reinterpret_cast<const SelSegDev*>(up.dev());
+    p.mode = mode;
+    p.threshold = threshold;
+    p.block_table = block_table;
+    p.block_table_numel = block_table_numel;
+    p.block_size = block_size;
+    p.out_idx = out_idx;
+    p.out_slot = out_slot;
+    p.out_count = out_count;
+    p.out_ld = out_ld;
+    p.err = dc.err_word;
+    launch_score_select(p, (cudaStream_t)stream);
+    up.finish((cudaStream_t)stream);
+  });
+}
+
+int daric_ptrs_to_slots(int64_t num_ranges, const int64_t* range_start, const int64_t* range_end,
+                        const int64_t* range_blk_off, const int32_t* block_table, int64_t block_table_numel,
+                        int64_t block_size, int32_t* out_idx, int64_t* out_slot, int device, void* stream) {
+  return guarded([&] {
+    if (num_ranges <= 0) return;
+    DARIC_CHECK(range_start && range_end && range_blk_off, "NULL range array");
+    DARIC_CHECK(block_size > 0, "block_size must be positive");
+    std::vector<RangeDev> rs;
+    rs.reserve(num_ranges);
+    int64_t total = 0;
+    for (int64_t r = 0; r < num_ranges; ++r) {
+      DARIC_CHECK(range_start[r] >= 0 && range_blk_off[r] >= 0, "negative range field at " + std::to_string(r));
+      DARIC_CHECK(range_end[r] <= INT32_MAX, "positions exceed int32");
+      if (range_end[r] <= range_start[r]) continue;
+      rs.push_back(RangeDev{range_start[r], range_end[r], range_blk_off[r], total});
+      total += range_end[r] - range_start[r];
+    }
+    if (total == 0) return;
+    DARIC_CHECK(out_idx && out_slot && block_table, "NULL device pointer");
+    DeviceCtx& dc = device_ctx(device);
+    DeviceGuard dg(device);
+    Upload up(dc, rs.size() * sizeof(RangeDev));
+    std::memcpy(up.host(), rs.data(), rs.size() * sizeof(RangeDev));
+    up.send(rs.size() * sizeof(RangeDev), (cudaStream_t)stream);
+    RangeLaunch p{};
+    p.ranges = reinterpret_cast<const RangeDev*>(up.dev());
+    p.num_ranges = (int64_t)rs.size();
+    p.total = total;
+    p.block_table = block_table;
+    p.block_table_numel = block_table_numel;
+    p.block_size = block_size;
+    p.out_idx = out_idx;
+    p.out_slot = out_slot;
+    p.err = dc.err_word;
+    launch_ranges_to_slots(p, (cudaStream_t)stream);
+    up.finish((cudaStream_t)stream);
+  });
+}
+
+}  // extern "C"

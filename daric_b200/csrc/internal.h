@@ -1,0 +1,222 @@
+// Internal definitions shared by the host side (capi.cpp) and the kernels.
+//
+// Device descriptors are uploaded once per call as one contiguous blob
+// (launch header, layer table, job table, chunk table) through a pinned ring
+// (desc_ring.cpp); kernels read them through __ldg-cached loads.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "../../include/daric_b200.h"
+
+namespace daric {
+
+// ---------------------------------------------------------------- errors --
+// Errors are thrown inside the library and turned into status codes at the C
+// boundary (capi.cpp). Messages follow the reference's TORCH_CHECK texts where
+// a reference check exists.
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define DARIC_CHECK(cond, msg)                                          \
+  do {                                                                  \
+    if (!(cond)) throw ::daric::Error(DARIC_ERR_INVALID, (msg));        \
+  } while (0)
+
+#define DARIC_CUDA(call)                                                         \
+  do {                                                                           \
+    cudaError_t e_ = (call);                                                     \
+    if (e_ != cudaSuccess)                                                       \
+      throw ::daric::Error(DARIC_ERR_CUDA, std::string("CUDA error at ") +       \
+                                               __FILE__ + ":" +                  \
+                                               std::to_string(__LINE__) + " - " + \
+                                               cudaGetErrorString(e_));          \
+  } while (0)
+
+// ------------------------------------------------------- fast division --
+// Division by a runtime-invariant positive divisor with one multiply-high
+// (Granlund & Montgomery, "Division by Invariant Integers using
+// Multiplication", PLDI 1994, round-up method). Valid for 0 <= n < 2^31.
+struct FastDiv {
+  uint32_t d;
+  uint32_t mul;
+  uint32_t shift;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f{d, 0, 0};
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  f.shift = s;
+  // mul = floor(2^32 * (2^s - d) / d) + 1
+  f.mul = (uint32_t)(((1ull << 32) * ((1ull << s) - d)) / d + 1);
+  return f;
+}
+
+__host__ __device__ __forceinline__ uint32_t fdiv(uint32_t n, FastDiv f) {
+#ifdef __CUDA_ARCH__
+  uint32_t hi = __umulhi(n, f.mul);
+#else
+  uint32_t hi = (uint32_t)(((uint64_t)n * f.mul) >> 32);
+#endif
+  return (uint32_t)(((uint64_t)hi + n) >> f.shift);
+}
+
+// ------------------------------------------------------------ layouts ----
+// One registered KV layer as the kernels see it.
+struct LayerDev {
+  uint8_t* base;          // layer data
+  int64_t page_stride;    // bytes between pages (blocks)
+  int64_t prefix_stride;  // bytes between prefix entries (K/V planes)
+  int64_t suffix;         // bytes of one (prefix, page) region (dense span)
+  int32_t prefix_size;
+  int32_t num_pages;
+  // rotation geometry (valid when has_rot)
+  int32_t has_rot;
+  int32_t k_prefix;       // prefix index whose region holds the K rows
+  int32_t nrows;          // K rows per page region
+  int32_t row_bytes;      // distance between consecutive K rows
+  int32_t row_vecs;       // row_bytes / 16
+  int32_t rot_vecs;       // 16-byte vectors of a row that are rotated
+  int32_t pair_vecs;      // rotation tasks per row (NeoX: rot_vecs/2, GPT-J: rot_vecs)
+  int32_t page_size;      // tokens per page
+  FastDiv pair_div;       // task -> row
+  FastDiv tok_div;        // row -> token (before the modulo)
+  FastDiv tok_mod;        // modulo page_size
+  FastDiv tail_div;       // row_vecs - rot_vecs (non-rotated vectors per row)
+  int32_t tail_vecs;      // row_vecs - rot_vecs
+  int32_t half_rot;       // rotary_dim / 2 (elements)
+  const uint8_t* table;   // cos_sin_cache
+  int64_t table_row;      // bytes per table row
+  int64_t max_pos;        // rows of the table
+};
+
+struct JobDev {
+  int64_t stg_off;     // byte offset into the store buffer
+  int64_t idx_off;     // first entry of this job's block ids in indices_flat
+  int64_t unit_begin;  // first unit (page) of this job within the launch
+  int32_t n_sel;       // pages of this job
+  int32_t layer;       // index into the launch's LayerDev table
+  int32_t meta;        // chunk index (-1 = none)
+  int32_t score_row;   // score row (-1 = no scores)
+};
+
+struct MetaDev {
+  int64_t pos_a;      // FLEXIBLE: old start; DELTA: delta
+  int64_t pos_b;      // FLEXIBLE: new start
+  int64_t len;        // tokens to rotate
+  int64_t score_col;  // first score column of the chunk
+  int32_t rotate;     // 0 = copy only (old == new, or mode NONE)
+  int32_t pad;
+};
+
+struct PageLaunch {
+  const LayerDev* layers;
+  const JobDev* jobs;
+  const MetaDev* metas;
+  const uint8_t* store;      // store (staging) base
+  uint8_t* store_mut;        // same, writable (gather)
+  const int32_t* indices;    // indices_flat
+  int64_t indices_numel;
+  int64_t num_jobs;
+  int64_t total_units;
+  int32_t mode;              // DARIC_ROPE_*
+  float* scores;
+  int64_t score_ld;
+  int* err;                  // device error word
+  size_t smem_bytes;         // dynamic shared memory of the rotating kernel
+};
+
+// In-place rotation segments.
+struct SegDev {
+  int64_t blk_off;     // offset of the request's block table
+  int64_t tok_start;   // first token position
+  int64_t tok_len;     // tokens
+  int64_t pos_a, pos_b;
+  int64_t unit_begin;  // first unit (page-slice) of the segment
+  int32_t first_page;  // tok_start / page_size
+  int32_t num_units;   // pages touched
+};
+
+struct InplaceLaunch {
+  const LayerDev* layers;
+  int64_t num_layers;
+  const SegDev* segs;
+  int64_t num_segs;
+  int64_t units_per_layer;   // sum over segments of pages touched
+  const int32_t* block_table;
+  int64_t block_table_numel;
+  int32_t mode;
+  int* err;
+  size_t smem_bytes;
+};
+
+// Dynamic shared memory of the rotating kernels for one layer geometry:
+// factors (float2 per slot and frequency), slot flags and deviations.
+inline size_t rotate_smem_bytes(int page_size, int half_rot) {
+  return (size_t)page_size * half_rot * 8 + (size_t)page_size * 8;
+}
+
+struct SelSegDev {
+  int64_t col_off, len, pos0, k, blk_off, out_off;
+};
+
+struct SelectLaunch {
+  const float* scores;
+  int64_t num_layers, score_ld, num_segs;
+  const SelSegDev* segs;
+  int32_t mode;
+  float threshold;
+  const int32_t* block_table;
+  int64_t block_table_numel;
+  int64_t block_size;
+  int32_t* out_idx;
+  int64_t* out_slot;
+  int32_t* out_count;
+  int64_t out_ld;
+  int* err;
+};
+
+struct RangeDev {
+  int64_t start, end, blk_off, out_begin;
+};
+
+struct RangeLaunch {
+  const RangeDev* ranges;
+  int64_t num_ranges, total;
+  const int32_t* block_table;
+  int64_t block_table_numel;
+  int64_t block_size;
+  int32_t* out_idx;
+  int64_t* out_slot;
+  int* err;
+};
+
+// Device error bits (OR-ed into the device error word).
+enum : int {
+  DEV_ERR_BLOCK_RANGE = 1,   // a block id outside [0, num_pages)
+  DEV_ERR_TABLE_RANGE = 2,   // a rotary position outside [0, max_position)
+  DEV_ERR_INDEX_RANGE = 4,   // a block-table index outside the given table
+};
+
+// ------------------------------------------------------------ launchers --
+// Kernel signature key for the rotating scatter.
+struct RotKey {
+  int kv_dtype, tab_dtype, neox;
+};
+
+void launch_plain_pages(const PageLaunch& p, bool gather, bool vec16, int sm_count, cudaStream_t s);
+void launch_rotate_scatter(const PageLaunch& p, RotKey key, int sm_count, cudaStream_t s);
+void launch_rotate_inplace(const InplaceLaunch& p, RotKey key, int sm_count, cudaStream_t s);
+void launch_score_select(const SelectLaunch& p, cudaStream_t s);
+void launch_ranges_to_slots(const RangeLaunch& p, cudaStream_t s);
+
+int* device_error_word(int device);  // per-device error word (lazily created)
+
+}  // namespace daric

@@ -1,0 +1,206 @@
+"""GPU parity of the page kernels against the CPU oracle (bit-exact):
+scatter_pages / gather_pages (reference kernels.cu) and the fused
+rerotate_scatter_pages (scatter + adapter.py re-rotation)."""
+import numpy as np
+import pytest
+import torch
+
+from daric_b200 import _lib
+from daric_b200.cache_ops import CacheCopier
+from daric_b200.reuse import build_load_plan, layer_block_bytes
+from daric_b200.topo import CacheTopo
+from gpu_util import (layout_shape, oracle_layer, random_values, table_tensor, unique_blocks, bytes_np,
+                      RAW_NP)
+from oracle import pages as P
+from oracle import rerotate as R
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(layout, dt, nb=24, bs=16, H=2, D=128, nlayers=2, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    shape, pf = layout_shape(layout, nb, bs, H, D)
+    names = [f"model.layers.{i}.self_attn.attn" for i in range(nlayers)]
+    layers = {n: random_values(shape, dt, g) for n in names}
+    topo = CacheTopo.single_group(names, bs, layer_block_bytes(layers[names[0]], pf), pf)
+    return g, layers, topo, pf
+
+
+@pytest.mark.parametrize("layout", ["5d", "5dpf", "4d", "3d"])
+@pytest.mark.parametrize("direction", ["scatter", "gather"])
+def test_plain_copy_matches_oracle(layout, direction):
+    g, layers, topo, pf = _setup(layout, "bf16")
+    rng = np.random.default_rng(1)
+    blocks = unique_blocks(rng, 24, [3, 5, 2], with_null=True)
+    copier = CacheCopier()
+    for n, t in layers.items():
+        copier.register_layer(n, t, pf)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    plan = build_load_plan(topo, bpb, [(b,) for b in blocks], "cuda", base_offset=64)
+    store = torch.randint(0, 255, (plan.total_bytes + 128,), dtype=torch.uint8, generator=g).cuda()
+    copier.register_store(store)
+    ol = {n: oracle_layer(t, "bf16", pf)[0] for n, t in layers.items()}
+    st = bytes_np(store)
+    idx = plan.indices_flat.cpu().numpy()
+    args = (plan.layer_names, plan.offsets.tolist(), plan.byte_sizes.tolist(), plan.indices_flat,
+            plan.indices_offsets.tolist())
+    if direction == "scatter":
+        copier.scatter_pages(*args)
+        P.scatter_pages(ol, st, plan.layer_names, plan.offsets, plan.byte_sizes, idx, plan.indices_offsets)
+        torch.cuda.synchronize()
+        for n, t in layers.items():
+            np.testing.assert_array_equal(bytes_np(t), ol[n].mem)
+    else:
+        copier.gather_pages(*args)
+        P.gather_pages(ol, st, plan.layer_names, plan.offsets, plan.byte_sizes, idx, plan.indices_offsets)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(bytes_np(store), st)
+    assert _lib.device_errors(0) == 0
+
+
+def test_plain_copy_unaligned_byte_path():
+    # 3-D layer with 30-byte pages: not 16-byte aligned -> byte-granular kernel
+    g = torch.Generator().manual_seed(3)
+    t = random_values((9, 3, 5), "bf16", g, outliers=False)
+    copier = CacheCopier()
+    copier.register_layer("l", t, True)
+    suffix = 3 * 5 * 2
+    store = torch.randint(0, 255, (7 + 4 * suffix,), dtype=torch.uint8, generator=g).cuda()
+    copier.register_store(store)
+    ids = torch.tensor([4, 0, 8, 2], dtype=torch.int32, device="cuda")
+    ol = {"l": oracle_layer(t, "bf16", True)[0]}
+    st = bytes_np(store)
+    copier.scatter_pages(["l"], [7], [4 * suffix], ids, [0, 4])
+    P.scatter_pages(ol, st, ["l"], [7], [4 * suffix], ids.cpu().numpy(), [0, 4])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(bytes_np(t), ol["l"].mem)
+
+
+def test_copy_argument_errors_match_reference():
+    g, layers, topo, pf = _setup("5d", "bf16", nb=8)
+    copier = CacheCopier()
+    n = next(iter(layers))
+    copier.register_layer(n, layers[n], pf)
+    ids = torch.tensor([1, 2], dtype=torch.int32, device="cuda")
+    with pytest.raises(RuntimeError, match="store buffer not registered"):
+        copier.scatter_pages([n], [0], [0], ids, [0, 2])
+    store = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    copier.register_store(store)
+    with pytest.raises(RuntimeError, match="byte_size mismatch at job 0"):
+        copier.scatter_pages([n], [0], [123], ids, [0, 2])
+    with pytest.raises(RuntimeError, match="layer not registered"):
+        copier.scatter_pages(["nope"], [0], [0], ids, [0, 2])
+    with pytest.raises(RuntimeError, match="indices_flat must be int32"):
+        copier.scatter_pages([n], [0], [0], ids.long(), [0, 2])
+    with pytest.raises(RuntimeError, match="store range out of bounds"):
+        copier.scatter_pages([n], [(1 << 20) - 10], [2 * 2 * 16 * 2 * 128 * 2], ids, [0, 2])
+    with pytest.raises(RuntimeError, match="indices_offsets size"):
+        copier.scatter_pages([n], [0], [0], ids, [0])
+
+
+def test_out_of_range_block_is_skipped_and_flagged():
+    g, layers, topo, pf = _setup("5d", "bf16", nb=8, nlayers=1)
+    n, t = next(iter(layers.items()))
+    before = bytes_np(t)
+    copier = CacheCopier()
+    copier.register_layer(n, t, pf)
+    page = 2 * 16 * 2 * 128 * 2
+    store = torch.zeros(2 * page, dtype=torch.uint8, device="cuda")
+    copier.register_store(store)
+    ids = torch.tensor([99], dtype=torch.int32, device="cuda")  # >= num_pages
+    _lib.device_errors(0)
+    copier.scatter_pages([n], [0], [page], ids, [0, 1])
+    assert _lib.device_errors(0) & 1
+    np.testing.assert_array_equal(bytes_np(t), before)
+
+
+# ------------------------------------------------------------------ fused --
+def _fused_case(layout, dt, tab_dt, neox, rot_dim, mode, H=2, D=128, bs=16, seed=0, scores=True):
+    g, layers, topo, pf = _setup(layout, dt, nb=40, bs=bs, H=H, D=D, seed=seed)
+    rng = np.random.default_rng(seed)
+    lens = [32, 40, 16, 48, 5]          # partial pages in chunks 1 and 4
+    counts = [(n + bs - 1) // bs for n in lens]
+    blocks = unique_blocks(rng, 40, counts, with_null=True)
+    max_pos = 600
+    table, table_raw = table_tensor(max_pos, rot_dim, 5e5, tab_dt)
+    copier = CacheCopier()
+    for n, t in layers.items():
+        copier.register_layer(n, t, pf)
+        copier.register_rotary(n, table, rot_dim, neox)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    plan = build_load_plan(topo, bpb, [(b,) for b in blocks], "cuda", base_offset=32)
+    nelem = (plan.total_bytes + 64) // torch.empty(0, dtype=layers[plan.layer_names[0]].dtype).element_size()
+    store = random_values((nelem,), dt, g, outliers=False).view(torch.uint8).reshape(-1)
+    copier.register_store(store)
+    if mode == "flexible":
+        pos_a = [0, 7, 300, 100, 550]      # saved positions
+        pos_b = [50, 7, 10, 400, 500]      # new positions (chunk 1: old == new -> copy)
+    else:
+        pos_a = [16, 0, 300, 99, 583]      # deltas
+        pos_b = None
+    # oracle
+    ol = {n: oracle_layer(t, dt, pf) for n, t in layers.items()}
+    st = bytes_np(store)
+    idx = plan.indices_flat.cpu().numpy()
+    P.scatter_pages({n: v[0] for n, v in ol.items()}, st, plan.layer_names, plan.offsets, plan.byte_sizes, idx,
+                    plan.indices_offsets)
+    rot = R.Rotary(table_raw.reshape(max_pos, rot_dim), tab_dt, rot_dim, neox)
+    T = sum(lens)
+    col = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    exp_scores = np.zeros((len(layers), T), np.float32)
+    for j, (name, m) in enumerate(zip(plan.layer_names, plan.job_meta)):
+        li = int(plan.job_layer[j])
+        n_tok = lens[m]
+        if mode == "flexible" and pos_a[m] == pos_b[m]:
+            continue
+        ids = np.asarray(blocks[m], np.int64)
+        t = np.arange(n_tok)
+        keep = ids[t // bs] != 0
+        t = t[keep]
+        gidx = ids[t // bs] * bs + t % bs
+        if mode == "flexible":
+            c, s = R.flexible_factors(rot, pos_a[m] + t, pos_b[m] + t)
+        else:
+            c, s = R.delta_factors(rot, np.full(len(t), pos_a[m]))
+        dev = R.rotate_tokens(ol[name][1], rot, gidx, c, s)
+        exp_scores[li, col[m] + t] = dev
+    sc = torch.full((len(layers), T), -1.0, device="cuda") if scores else None
+    kw = dict(scores=sc, job_score_row=plan.job_layer, meta_score_col=col) if scores else {}
+    copier.rerotate_scatter_pages(plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat,
+                                  plan.indices_offsets, plan.job_meta, mode, pos_a, pos_b, lens, **kw)
+    torch.cuda.synchronize()
+    assert _lib.device_errors(0) == 0
+    for n, t in layers.items():
+        got = bytes_np(t).view(RAW_NP[dt])
+        exp = ol[n][0].mem.view(RAW_NP[dt])
+        bad = np.nonzero(got != exp)[0]
+        assert bad.size == 0, f"{bad.size} elements differ, first {bad[:5]}: {got[bad[:5]]} vs {exp[bad[:5]]}"
+    if scores:
+        np.testing.assert_allclose(sc.cpu().numpy(), exp_scores, rtol=1e-3, atol=1e-6)
+
+
+@pytest.mark.parametrize("mode", ["flexible", "delta"])
+@pytest.mark.parametrize("layout", ["5d", "5dpf", "4d", "3d"])
+def test_fused_bf16_neox_layouts(layout, mode):
+    _fused_case(layout, "bf16", "bf16", True, 128, mode)
+
+
+@pytest.mark.parametrize("dt,tab", [("f16", "f16"), ("f32", "f32"), ("fp8", "bf16"), ("bf16", "f32")])
+@pytest.mark.parametrize("mode", ["flexible", "delta"])
+def test_fused_dtypes(dt, tab, mode):
+    _fused_case("5d", dt, tab, True, 128, mode)
+
+
+@pytest.mark.parametrize("neox,rot_dim", [(False, 128), (True, 64), (False, 64)])
+def test_fused_gptj_and_partial_rotary(neox, rot_dim):
+    _fused_case("5d", "bf16", "bf16", neox, rot_dim, "flexible", seed=3)
+    _fused_case("4d", "bf16", "bf16", neox, rot_dim, "delta", seed=4)
+
+
+@pytest.mark.parametrize("H,D,bs", [(8, 128, 16), (4, 128, 32), (1, 64, 16), (8, 256, 8)])
+def test_fused_head_shapes(H, D, bs):
+    _fused_case("5d", "bf16", "bf16", True, D, "flexible", H=H, D=D, bs=bs, seed=H + D)
+
+
+def test_fused_without_scores():
+    _fused_case("5d", "bf16", "bf16", True, 128, "flexible", scores=False)
