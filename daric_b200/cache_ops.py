@@ -17,6 +17,7 @@ import ctypes as C
 from collections.abc import Sequence
 from typing import Optional
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -300,6 +301,18 @@ def _as_uint8_ptr(t: torch.Tensor, what: str) -> int:
     return t.data_ptr()
 
 
+def _check_regions(a: torch.Tensor, a_off, b: torch.Tensor, b_off, sizes) -> None:
+    # The reference does not bound-check these regions; a bad region here
+    # raises instead of letting the copy engine touch foreign memory.
+    z = np.asarray(sizes, np.int64)
+    for t, off, what in ((a, a_off, "source"), (b, b_off, "destination")):
+        o = np.asarray(off, np.int64)
+        if len(o) != len(z):
+            raise RuntimeError("offsets and sizes must have the same length")
+        if len(z) and ((o < 0).any() or (z < 0).any() or (o + z).max() > t.numel()):
+            raise RuntimeError(f"copy region outside the {what} buffer")
+
+
 def batched_memcpy_d2h(staging: torch.Tensor, shm: torch.Tensor, stg_offsets: Sequence[int],
                        shm_offsets: Sequence[int], sizes: Sequence[int], stream: int = 0) -> None:
     """One copy-engine cudaMemcpyAsync (D2H) per region (helpers.cu:187-217).
@@ -307,6 +320,7 @@ def batched_memcpy_d2h(staging: torch.Tensor, shm: torch.Tensor, stg_offsets: Se
     n = len(sizes)
     if n == 0:
         return
+    _check_regions(staging, stg_offsets, shm, shm_offsets, sizes)
     src = _as_uint8_ptr(staging, "staging")
     dst = _as_uint8_ptr(shm, "shm")
     dev = staging.device.index if staging.is_cuda else torch.cuda.current_device()
@@ -324,6 +338,7 @@ def batched_memcpy_h2d(shm: torch.Tensor, staging: torch.Tensor, shm_offsets: Se
     n = len(sizes)
     if n == 0:
         return
+    _check_regions(shm, shm_offsets, staging, stg_offsets, sizes)
     src = _as_uint8_ptr(shm, "shm")
     dst = _as_uint8_ptr(staging, "staging")
     dev = staging.device.index if staging.is_cuda else torch.cuda.current_device()

@@ -826,12 +826,11 @@ int daric_score_select(const float* scores, int64_t num_layers, int64_t score_ld
       d.out_off = out_off[s];
       DARIC_CHECK(d.col_off >= 0 && d.len >= 0 && d.pos0 >= 0 && d.k >= 0 && d.blk_off >= 0 && d.out_off >= 0,
                   "negative segment field at segment " + std::to_string(s));
-      DARIC_CHECK(d.col_off + d.len <= score_ld || num_layers == 1,
-                  "segment " + std::to_string(s) + " exceeds the score row");
+      DARIC_CHECK(d.col_off + d.len <= score_ld,
+                  "segment " + std::to_string(s) + " exceeds the score row (score_ld)");
       DARIC_CHECK(d.pos0 + d.len <= INT32_MAX, "positions exceed int32");
       const int64_t cap = mode == DARIC_SELECT_TOPK ? std::min(d.k, d.len) : d.len;
-      DARIC_CHECK(d.out_off + cap <= out_ld || num_layers == 1,
-                  "segment " + std::to_string(s) + " output exceeds out_ld");
+      DARIC_CHECK(d.out_off + cap <= out_ld, "segment " + std::to_string(s) + " output exceeds out_ld");
     }
     DeviceCtx& dc = device_ctx(device);
     DeviceGuard dg(device);

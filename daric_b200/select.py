@@ -62,6 +62,8 @@ def score_select(scores: torch.Tensor, block_table: torch.Tensor, block_size: in
     nseg = len(seg_len)
     lens, lp = i64(seg_len)
     cols, cp = i64(seg_col_off if seg_col_off is not None else np.concatenate([[0], np.cumsum(lens)[:-1]]))
+    if len(cols) != nseg or (nseg and (cols.min() < 0 or (cols + lens).max() > T)):
+        raise RuntimeError("score segments must lie inside the score rows")
     pos0, pp = i64(seg_pos0 if seg_pos0 is not None else [0] * nseg)
     blk, bp = i64(seg_blk_off if seg_blk_off is not None else [0] * nseg)
     if threshold is not None:
