@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -76,6 +77,7 @@ struct RingSlot {
 struct DeviceCtx {
   int device = -1;
   int sm_count = 0;
+  int smem_optin = 0;
   int* err_word = nullptr;
   std::mutex mu;
   unsigned next = 0;
@@ -92,6 +94,7 @@ DeviceCtx& device_ctx(int device) {
   auto c = std::make_unique<DeviceCtx>();
   c->device = device;
   DARIC_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
+  DARIC_CUDA(cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
   DeviceGuard dg(device);
   DARIC_CUDA(cudaMalloc(&c->err_word, sizeof(int)));
   DARIC_CUDA(cudaMemset(c->err_word, 0, sizeof(int)));
@@ -366,6 +369,35 @@ JobPlan plan_jobs(daric_copier* c, int64_t num_jobs, const char* const* names, c
   return jp;
 }
 
+// Page-kernel choice: the bulk-copy pipeline unless DARIC_PAGE_KERNEL=simt
+// (diagnostic switch for A/B measurements of the two implementations).
+bool bulk_pipeline_enabled() {
+  const char* v = std::getenv("DARIC_PAGE_KERNEL");
+  return !(v && std::strcmp(v, "simt") == 0);
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Bulk pipeline geometry for a launch, or nstage = 0 when a unit does not
+// fit two shared-memory stages.
+BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate) {
+  BulkGeom g{};
+  size_t stage = 0, fac = 0;
+  for (const auto& l : layers) {
+    stage = std::max(stage, (size_t)l.prefix_size * (size_t)l.suffix);
+    if (rotate) fac = std::max(fac, rotate_smem_bytes(l.page_size, l.half_rot));
+  }
+  stage = round_up(stage, 128);
+  fac = round_up(fac, 128);
+  if (stage == 0 || stage >= (1u << 20) || (size_t)dc.smem_optin < 256 + fac) return g;
+  const size_t ns = std::min<size_t>(4, ((size_t)dc.smem_optin - 256 - fac) / stage);
+  if (ns < 2) return g;
+  g.nstage = (int32_t)ns;
+  g.stage_bytes = (int32_t)stage;
+  g.fac_bytes = (int32_t)fac;
+  return g;
+}
+
 // Builds and launches page jobs. mode/metas only for the rotating scatter.
 void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t>& job_index,
                    const int64_t* offsets, const int32_t* indices_flat, int64_t indices_numel,
@@ -424,8 +456,15 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   p.err = dc.err_word;
   p.smem_bytes = 0;
   for (const auto& l : layers) p.smem_bytes = std::max(p.smem_bytes, rotate_smem_bytes(l.page_size, l.half_rot));
-  if (rotate) launch_rotate_scatter(p, key, dc.sm_count, stream);
-  else launch_plain_pages(p, gather, jp.vec16, dc.sm_count, stream);
+  const BulkGeom bg = (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate) : BulkGeom{};
+  if (bg.nstage >= 2) {
+    if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
+    else launch_bulk_plain(p, bg, gather, dc.sm_count, stream);
+  } else if (rotate) {
+    launch_rotate_scatter(p, key, dc.sm_count, stream);
+  } else {
+    launch_plain_pages(p, gather, jp.vec16, dc.sm_count, stream);
+  }
   up.finish(stream);
 }
 

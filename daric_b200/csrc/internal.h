@@ -203,7 +203,21 @@ enum : int {
   DEV_ERR_BLOCK_RANGE = 1,   // a block id outside [0, num_pages)
   DEV_ERR_TABLE_RANGE = 2,   // a rotary position outside [0, max_position)
   DEV_ERR_INDEX_RANGE = 4,   // a block-table index outside the given table
+  DEV_ERR_TIMEOUT = 8,       // a bounded wait in a pipelined kernel gave up
 };
+
+// Geometry of the bulk-copy pipeline: NSTAGE shared-memory stages of
+// stage_bytes each, after a fac_bytes rotation-state region.
+struct BulkGeom {
+  int32_t nstage;
+  int32_t stage_bytes;
+  int32_t fac_bytes;
+  int32_t pad;
+};
+
+inline size_t bulk_smem_bytes(const BulkGeom& g) {
+  return 256 + (size_t)g.fac_bytes + (size_t)g.nstage * g.stage_bytes;
+}
 
 // ------------------------------------------------------------ launchers --
 // Kernel signature key for the rotating scatter.
@@ -214,6 +228,8 @@ struct RotKey {
 void launch_plain_pages(const PageLaunch& p, bool gather, bool vec16, int sm_count, cudaStream_t s);
 void launch_rotate_scatter(const PageLaunch& p, RotKey key, int sm_count, cudaStream_t s);
 void launch_rotate_inplace(const InplaceLaunch& p, RotKey key, int sm_count, cudaStream_t s);
+void launch_bulk_plain(const PageLaunch& p, const BulkGeom& g, bool gather, int sm_count, cudaStream_t s);
+void launch_bulk_rotate(const PageLaunch& p, const BulkGeom& g, RotKey key, int sm_count, cudaStream_t s);
 void launch_score_select(const SelectLaunch& p, cudaStream_t s);
 void launch_ranges_to_slots(const RangeLaunch& p, cudaStream_t s);
 

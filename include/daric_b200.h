@@ -65,7 +65,8 @@ DARIC_API int daric_device_sm_count(int device, int* out_sm_count);
 
 /* Reads and clears the device-side error bits of `device`: 1 = a block id
  * outside [0, num_pages) was skipped, 2 = a rotary position outside the table
- * was skipped, 4 = a block-table index outside the given table was skipped.
+ * was skipped, 4 = a block-table index outside the given table was skipped,
+ * 8 = a bounded wait inside a pipelined kernel gave up (its unit was dropped).
  * The kernels never fault on these; they skip the access and set the bit.
  * Synchronous (waits for the device's work to finish). */
 DARIC_API int daric_device_errors(int device, int* out_bits);

@@ -26,9 +26,20 @@ def _setup(layout, dt, nb=24, bs=16, H=2, D=128, nlayers=2, seed=0):
     return g, layers, topo, pf
 
 
+@pytest.fixture(params=["bulk", "simt"])
+def page_kernel(request, monkeypatch):
+    """Runs a test with each page-kernel implementation (bulk-copy pipeline
+    and SIMT vector kernel)."""
+    if request.param == "simt":
+        monkeypatch.setenv("DARIC_PAGE_KERNEL", "simt")
+    else:
+        monkeypatch.delenv("DARIC_PAGE_KERNEL", raising=False)
+    return request.param
+
+
 @pytest.mark.parametrize("layout", ["5d", "5dpf", "4d", "3d"])
 @pytest.mark.parametrize("direction", ["scatter", "gather"])
-def test_plain_copy_matches_oracle(layout, direction):
+def test_plain_copy_matches_oracle(layout, direction, page_kernel):
     g, layers, topo, pf = _setup(layout, "bf16")
     rng = np.random.default_rng(1)
     blocks = unique_blocks(rng, 24, [3, 5, 2], with_null=True)
@@ -181,24 +192,24 @@ def _fused_case(layout, dt, tab_dt, neox, rot_dim, mode, H=2, D=128, bs=16, seed
 
 @pytest.mark.parametrize("mode", ["flexible", "delta"])
 @pytest.mark.parametrize("layout", ["5d", "5dpf", "4d", "3d"])
-def test_fused_bf16_neox_layouts(layout, mode):
+def test_fused_bf16_neox_layouts(layout, mode, page_kernel):
     _fused_case(layout, "bf16", "bf16", True, 128, mode)
 
 
 @pytest.mark.parametrize("dt,tab", [("f16", "f16"), ("f32", "f32"), ("fp8", "bf16"), ("bf16", "f32")])
 @pytest.mark.parametrize("mode", ["flexible", "delta"])
-def test_fused_dtypes(dt, tab, mode):
+def test_fused_dtypes(dt, tab, mode, page_kernel):
     _fused_case("5d", dt, tab, True, 128, mode)
 
 
 @pytest.mark.parametrize("neox,rot_dim", [(False, 128), (True, 64), (False, 64)])
-def test_fused_gptj_and_partial_rotary(neox, rot_dim):
+def test_fused_gptj_and_partial_rotary(neox, rot_dim, page_kernel):
     _fused_case("5d", "bf16", "bf16", neox, rot_dim, "flexible", seed=3)
     _fused_case("4d", "bf16", "bf16", neox, rot_dim, "delta", seed=4)
 
 
-@pytest.mark.parametrize("H,D,bs", [(8, 128, 16), (4, 128, 32), (1, 64, 16), (8, 256, 8)])
-def test_fused_head_shapes(H, D, bs):
+@pytest.mark.parametrize("H,D,bs", [(8, 128, 16), (4, 128, 32), (1, 64, 16), (8, 256, 8), (8, 128, 64)])
+def test_fused_head_shapes(H, D, bs, page_kernel):
     _fused_case("5d", "bf16", "bf16", True, D, "flexible", H=H, D=D, bs=bs, seed=H + D)
 
 

@@ -1,0 +1,61 @@
+"""Bit-exact parity of scatter_pages / gather_pages with the reference's own
+compiled CUDA module (oracle/_ref, built by oracle/build_ref.py from the
+reference sources); skipped when that module was not built."""
+import numpy as np
+import pytest
+import torch
+
+from daric_b200.cache_ops import CacheCopier
+from daric_b200.reuse import build_load_plan, layer_block_bytes
+from daric_b200.topo import CacheTopo
+from gpu_util import layout_shape, random_values, unique_blocks
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from oracle.build_ref import load_ref
+    mod = load_ref()
+    if mod is None:
+        pytest.skip("reference module not built (oracle/build_ref.py)")
+    return mod
+
+
+@pytest.mark.parametrize("layout", ["5d", "5dpf", "4d"])
+@pytest.mark.parametrize("kernel", ["bulk", "simt"])
+def test_scatter_gather_match_reference_module(ref, layout, kernel, monkeypatch):
+    if kernel == "simt":
+        monkeypatch.setenv("DARIC_PAGE_KERNEL", "simt")
+    g = torch.Generator().manual_seed(11)
+    shape, pf = layout_shape(layout, 32, 16, 4, 128)
+    names = [f"model.layers.{i}.self_attn.attn" for i in range(3)]
+    base = {n: random_values(shape, "bf16", g) for n in names}
+    rng = np.random.default_rng(4)
+    blocks = unique_blocks(rng, 32, [4, 7, 3, 9], with_null=True)
+    topo = CacheTopo.single_group(names, 16, layer_block_bytes(base[names[0]], pf), pf)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in base.items()}
+    plan = build_load_plan(topo, bpb, [(b,) for b in blocks], "cuda", base_offset=48)
+    store0 = torch.randint(0, 255, (plan.total_bytes + 96,), dtype=torch.uint8, generator=g).cuda()
+    args = (plan.layer_names, plan.offsets.tolist(), plan.byte_sizes.tolist(), plan.indices_flat,
+            plan.indices_offsets.tolist())
+    outs = {}
+    for who, cls in (("ours", CacheCopier), ("ref", ref.CacheCopier)):
+        layers = {n: t.clone() for n, t in base.items()}
+        store = store0.clone()
+        c = cls()
+        for n, t in layers.items():
+            c.register_layer(n, t, pf)
+        c.register_store(store)
+        c.scatter_pages(*args)
+        torch.cuda.synchronize()
+        scattered = {n: t.clone() for n, t in layers.items()}
+        # gather back from freshly randomised layers into the store
+        for t in layers.values():
+            t.copy_(random_values(shape, "bf16", torch.Generator().manual_seed(5)))
+        c.gather_pages(*args)
+        torch.cuda.synchronize()
+        outs[who] = (scattered, store.clone())
+    for n in names:
+        assert torch.equal(outs["ours"][0][n].view(torch.int16), outs["ref"][0][n].view(torch.int16)), n
+    assert torch.equal(outs["ours"][1], outs["ref"][1])
