@@ -111,13 +111,15 @@ __device__ __forceinline__ int64_t find_job(const JobDev* jobs, int64_t n, int64
   return lo;
 }
 
-// Rotates the K rows of one region held in shared memory (in place).
-template <class E, bool NEOX>
-__device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kreg, PageSmem sm, bool scoring) {
+// Rotates the K rows of one region held in shared memory (in place) with
+// the page's factor block (also in shared memory).
+template <class E, bool NEOX, bool SCORE>
+__device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kreg, const float4* fac,
+                                                 int64_t tok0, int64_t len, float* tok_dev) {
   constexpr int U = 4;
-  constexpr int FPV = NEOX ? E::kPerVec : E::kPerVec / 2;
   const int ntask = L.nrows * L.pair_vecs;
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
+  const int per_tok = L.half_rot / 2;
   const uint32_t base = smem_addr(kreg);
   for (int b0 = threadIdx.x; b0 < ntask; b0 += U * blockDim.x) {
     uint4 lo[U], hi[U];
@@ -129,9 +131,8 @@ __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kre
       if (t < ntask) {
         const int row = (int)fdiv((uint32_t)t, L.pair_div);
         c[u] = t - row * L.pair_vecs;
-        const uint32_t q = fdiv((uint32_t)row, L.tok_div);
-        slot[u] = (int)(q - fdiv(q, L.tok_mod) * (uint32_t)L.page_size);
-        if (sm.ok[slot[u]]) {
+        slot[u] = row_slot(L, row);
+        if (tok0 + slot[u] < len) {
           off[u] = row * L.row_bytes + c[u] * 16;
           lo[u] = lds128(base + off[u]);
           if (NEOX) hi[u] = lds128(base + off[u] + hi_off);
@@ -141,27 +142,27 @@ __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kre
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       if (off[u] < 0) continue;
-      const float2* f = sm.fac + slot[u] * L.half_rot + c[u] * FPV;
+      const float4* q = fac + slot[u] * per_tok + c[u];
       float dv = 0.f;
-      if (NEOX) rotate_neox<E>(f, lo[u], hi[u], dv);
-      else rotate_gptj<E>(f, lo[u], dv);
-      if (scoring) atomicAdd(&sm.dev[slot[u]], dv);
+      if (NEOX) rotate_neox_q<E, SCORE>(q, L.pair_vecs, lo[u], hi[u], dv);
+      else rotate_gptj_q<E, SCORE>(q, L.pair_vecs, lo[u], dv);
+      if (SCORE) atomicAdd(&tok_dev[slot[u]], dv);
       sts128(base + off[u], lo[u]);
       if (NEOX) sts128(base + off[u] + hi_off, hi[u]);
     }
   }
 }
 
-// Shared memory: [0,64) barriers | [64,256) stage meta | fac region | stages.
-template <int KVT, int TABT, bool NEOX, bool ROTATE, bool GATHER>
+// Shared memory: [0,64) barriers | [64,256) stage meta | dev region |
+// stages (page data, then the page's factor block at fac_off).
+template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE>
 __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch p, BulkGeom g) {
   using E = Elem<KVT>;
-  using T = Elem<TABT>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   StageMeta* meta = reinterpret_cast<StageMeta*>(smem + 64);
-  uint8_t* facbase = smem + 256;
-  uint8_t* stages = smem + 256 + g.fac_bytes;
+  float* tok_dev = reinterpret_cast<float*>(smem + 256);
+  uint8_t* stages = smem + 256 + g.dev_bytes;
   const int NS = g.nstage;
   const int tid = threadIdx.x;
 
@@ -179,8 +180,11 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     if (GATHER) return p.store_mut + j.stg_off + ((int64_t)pf * j.n_sel + pl) * L.suffix;
     return L.base + (int64_t)pf * L.prefix_stride + (int64_t)blk * L.page_stride;
   };
+  auto unit_rotates = [&](const JobDev& j, const LayerDev& L) -> bool {
+    return ROTATE && j.meta >= 0 && L.has_rot && p.metas[j.meta].rotate;
+  };
   auto issue = [&](int64_t u, int s) {
-    while (pj + 1 < p.num_jobs && __ldg(&p.jobs[pj + 1].unit_begin) <= u) ++pj;
+    while (pj + 1 < p.num_jobs && p.jobs[pj + 1].unit_begin <= u) ++pj;
     const JobDev j = p.jobs[pj];
     const LayerDev& L = p.layers[j.layer];
     const int64_t pl = u - j.unit_begin;
@@ -196,9 +200,13 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       return;
     }
     uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-    mbar_arrive_expect_tx(&bars[s], (uint32_t)(L.prefix_size * L.suffix));
+    const bool rot = unit_rotates(j, L);
+    const uint32_t fbytes = rot ? (uint32_t)page_factor_bytes(L.page_size, L.half_rot) : 0u;
+    mbar_arrive_expect_tx(&bars[s], (uint32_t)(L.prefix_size * L.suffix) + fbytes);
     for (int pf = 0; pf < L.prefix_size; ++pf)
       bulk_load(buf + (size_t)pf * L.suffix, region_src(j, L, pl, blk, pf), (uint32_t)L.suffix, &bars[s]);
+    if (rot)
+      bulk_load(buf + g.fac_off, p.fac + (j.fac_tok + pl * L.page_size) * (L.half_rot / 2), fbytes, &bars[s]);
   };
 
   if (tid == 0) {
@@ -217,21 +225,20 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     const JobDev j = p.jobs[st.job];
     const LayerDev& L = p.layers[j.layer];
     uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-    MetaDev m{};
-    if (ROTATE && j.meta >= 0) m = p.metas[j.meta];
-    const bool rotate = ROTATE && j.meta >= 0 && m.rotate && L.has_rot && !st.skip;
-    const bool scoring = ROTATE && p.scores != nullptr && j.score_row >= 0 && j.meta >= 0;
-    const PageSmem sm = page_smem(facbase, L);
+    const bool rotate = !st.skip && unit_rotates(j, L);
+    const bool scoring = SCORE && j.score_row >= 0 && j.meta >= 0;
+    const int64_t len = (ROTATE && j.meta >= 0) ? p.metas[j.meta].len : 0;
     const int64_t tok0 = st.page_local * L.page_size;
     if (scoring)
-      for (int q = tid; q < L.page_size; q += blockDim.x) sm.dev[q] = 0.f;
-    if (rotate) fill_factors<T>(L, p.mode, m.pos_a, m.pos_b, tok0, m.len, sm, p.err);
+      for (int q = tid; q < L.page_size; q += blockDim.x) tok_dev[q] = 0.f;
     const bool ok = mbar_wait(&bars[s], (uint32_t)((i / NS) & 1));
     if (__syncthreads_or(!ok)) {
       failed = true;
       break;
     }
-    if (rotate) rotate_rows_smem<E, NEOX>(L, buf + (size_t)L.k_prefix * L.suffix, sm, scoring);
+    if (rotate)
+      rotate_rows_smem<E, NEOX, SCORE>(L, buf + (size_t)L.k_prefix * L.suffix,
+                                       reinterpret_cast<const float4*>(buf + g.fac_off), tok0, len, tok_dev);
     fence_proxy_async();
     __syncthreads();
     if (tid == 0 && !st.skip) {
@@ -240,9 +247,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       bulk_commit();
     }
     if (scoring) {
-      float* out = p.scores + (int64_t)j.score_row * p.score_ld + m.score_col + tok0;
+      float* out = p.scores + (int64_t)j.score_row * p.score_ld + p.metas[j.meta].score_col + tok0;
       for (int q = tid; q < L.page_size; q += blockDim.x)
-        if (tok0 + q < m.len) out[q] = st.skip ? 0.f : sm.dev[q];
+        if (tok0 + q < len) out[q] = rotate ? tok_dev[q] : 0.f;
     }
     // Unit i+NS-1 reuses the stage of unit i-1, whose stores must have
     // finished reading it (the newest bulk group, unit i's, may still run).
@@ -281,37 +288,33 @@ void launch_bulk(K kernel, const PageLaunch& p, const BulkGeom& g, int sm_count,
   DARIC_CUDA(cudaGetLastError());
 }
 
-template <int KVT, int TABT>
-void bulk_rotate(const PageLaunch& p, const BulkGeom& g, bool neox, int sm, cudaStream_t s) {
-  if (neox) launch_bulk(bulk_pages_kernel<KVT, TABT, true, true, false>, p, g, sm, s);
-  else launch_bulk(bulk_pages_kernel<KVT, TABT, false, true, false>, p, g, sm, s);
-}
-
 template <int KVT>
-void bulk_rotate_tab(const PageLaunch& p, const BulkGeom& g, int tab, bool neox, int sm, cudaStream_t s) {
-  switch (tab) {
-    case DARIC_DTYPE_BF16: return bulk_rotate<KVT, DARIC_DTYPE_BF16>(p, g, neox, sm, s);
-    case DARIC_DTYPE_F16: return bulk_rotate<KVT, DARIC_DTYPE_F16>(p, g, neox, sm, s);
-    case DARIC_DTYPE_F32: return bulk_rotate<KVT, DARIC_DTYPE_F32>(p, g, neox, sm, s);
+void bulk_rotate(const PageLaunch& p, const BulkGeom& g, bool neox, int sm, cudaStream_t s) {
+  const bool sc = p.scores != nullptr;
+  if (neox) {
+    if (sc) launch_bulk(bulk_pages_kernel<KVT, true, true, false, true>, p, g, sm, s);
+    else launch_bulk(bulk_pages_kernel<KVT, true, true, false, false>, p, g, sm, s);
+  } else {
+    if (sc) launch_bulk(bulk_pages_kernel<KVT, false, true, false, true>, p, g, sm, s);
+    else launch_bulk(bulk_pages_kernel<KVT, false, true, false, false>, p, g, sm, s);
   }
-  throw Error(DARIC_ERR_INVALID, "unsupported rotary table dtype");
 }
 
 }  // namespace
 
 void launch_bulk_plain(const PageLaunch& p, const BulkGeom& g, bool gather, int sm, cudaStream_t s) {
   if (gather)
-    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, DARIC_DTYPE_BF16, true, false, true>, p, g, sm, s);
+    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, true, false, true, false>, p, g, sm, s);
   else
-    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, DARIC_DTYPE_BF16, true, false, false>, p, g, sm, s);
+    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, true, false, false, false>, p, g, sm, s);
 }
 
 void launch_bulk_rotate(const PageLaunch& p, const BulkGeom& g, RotKey k, int sm, cudaStream_t s) {
   switch (k.kv_dtype) {
-    case DARIC_DTYPE_BF16: return bulk_rotate_tab<DARIC_DTYPE_BF16>(p, g, k.tab_dtype, k.neox, sm, s);
-    case DARIC_DTYPE_F16: return bulk_rotate_tab<DARIC_DTYPE_F16>(p, g, k.tab_dtype, k.neox, sm, s);
-    case DARIC_DTYPE_F32: return bulk_rotate_tab<DARIC_DTYPE_F32>(p, g, k.tab_dtype, k.neox, sm, s);
-    case DARIC_DTYPE_FP8_E4M3: return bulk_rotate_tab<DARIC_DTYPE_FP8_E4M3>(p, g, k.tab_dtype, k.neox, sm, s);
+    case DARIC_DTYPE_BF16: return bulk_rotate<DARIC_DTYPE_BF16>(p, g, k.neox, sm, s);
+    case DARIC_DTYPE_F16: return bulk_rotate<DARIC_DTYPE_F16>(p, g, k.neox, sm, s);
+    case DARIC_DTYPE_F32: return bulk_rotate<DARIC_DTYPE_F32>(p, g, k.neox, sm, s);
+    case DARIC_DTYPE_FP8_E4M3: return bulk_rotate<DARIC_DTYPE_FP8_E4M3>(p, g, k.neox, sm, s);
   }
   throw Error(DARIC_ERR_INVALID, "unsupported KV dtype");
 }

@@ -70,6 +70,8 @@ struct RingSlot {
   uint8_t* host = nullptr;
   uint8_t* dev = nullptr;
   size_t cap = 0;
+  uint8_t* scratch = nullptr;  // device scratch of the call (rotary factors)
+  size_t scratch_cap = 0;
   cudaEvent_t done = nullptr;
   bool pending = false;
 };
@@ -132,6 +134,18 @@ class Upload {
   }
   uint8_t* host() { return slot_->host; }
   uint8_t* dev() { return slot_->dev; }
+  // Device scratch owned by this slot until finish(); grown on demand.
+  uint8_t* scratch(size_t bytes) {
+    if (slot_->scratch_cap < bytes) {
+      if (slot_->scratch) DARIC_CUDA(cudaFree(slot_->scratch));
+      slot_->scratch = nullptr;
+      slot_->scratch_cap = 0;
+      const size_t cap = std::max(bytes, slot_->scratch_cap * 2);
+      DARIC_CUDA(cudaMalloc((void**)&slot_->scratch, cap));
+      slot_->scratch_cap = cap;
+    }
+    return slot_->scratch;
+  }
   void send(size_t bytes, cudaStream_t s) {
     if (bytes) DARIC_CUDA(cudaMemcpyAsync(slot_->dev, slot_->host, bytes, cudaMemcpyHostToDevice, s));
   }
@@ -378,24 +392,33 @@ bool bulk_pipeline_enabled() {
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Bulk pipeline geometry for a launch, or nstage = 0 when a unit does not
-// fit two shared-memory stages.
-BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate) {
+// Bulk pipeline geometry for a launch, or nstage = 0 when a unit (page data
+// plus, when rotating, its factor block) does not fit two stages.
+BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores) {
   BulkGeom g{};
-  size_t stage = 0, fac = 0;
+  size_t data = 0, fac = 0, dev = 0;
   for (const auto& l : layers) {
-    stage = std::max(stage, (size_t)l.prefix_size * (size_t)l.suffix);
-    if (rotate) fac = std::max(fac, rotate_smem_bytes(l.page_size, l.half_rot));
+    data = std::max(data, (size_t)l.prefix_size * (size_t)l.suffix);
+    if (rotate) fac = std::max(fac, page_factor_bytes(l.page_size, l.half_rot));
+    if (scores) dev = std::max(dev, (size_t)l.page_size * 4);
   }
-  stage = round_up(stage, 128);
-  fac = round_up(fac, 128);
-  if (stage == 0 || stage >= (1u << 20) || (size_t)dc.smem_optin < 256 + fac) return g;
-  const size_t ns = std::min<size_t>(4, ((size_t)dc.smem_optin - 256 - fac) / stage);
+  const size_t fac_off = round_up(data, 128);
+  const size_t stage = round_up(fac_off + fac, 128);
+  dev = round_up(dev, 128);
+  if (data == 0 || data + fac >= (1u << 20) || (size_t)dc.smem_optin < 256 + dev) return g;
+  const size_t ns = std::min<size_t>(4, ((size_t)dc.smem_optin - 256 - dev) / stage);
   if (ns < 2) return g;
   g.nstage = (int32_t)ns;
   g.stage_bytes = (int32_t)stage;
-  g.fac_bytes = (int32_t)fac;
+  g.fac_off = (int32_t)fac_off;
+  g.dev_bytes = (int32_t)dev;
   return g;
+}
+
+// Elements of a 16-byte vector / factors per rotation task of a layer.
+int factors_per_task(int kv_dtype, bool neox) {
+  const int epv = 16 / dtype_size(kv_dtype);
+  return neox ? epv : epv / 2;
 }
 
 // Builds and launches page jobs. mode/metas only for the rotating scatter.
@@ -408,14 +431,20 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   // Layer table restricted to this launch's layers.
   std::vector<int> slot_map(jp.uniq.size(), -1);
   std::vector<LayerDev> layers;
+  std::vector<const LayerHost*> lhost;
   std::vector<JobDev> jobs;
   jobs.reserve(job_index.size());
+  // Factor runs: one per (rotating chunk, rotary table), padded to whole pages.
+  std::map<std::pair<int64_t, const void*>, size_t> run_of;
+  std::vector<FacJobDev> runs;
+  std::vector<int64_t> run_tokens;  // padded token count of each run
   int64_t units = 0;
   for (int64_t i : job_index) {
     const int us = jp.layer_slot[i];
     if (slot_map[us] < 0) {
       slot_map[us] = (int)layers.size();
       layers.push_back(base_layer_dev(*jp.uniq[us]));
+      lhost.push_back(jp.uniq[us]);
     }
     if (jp.n_sel[i] == 0) continue;
     JobDev j{};
@@ -426,20 +455,80 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
     j.layer = slot_map[us];
     j.meta = rotate ? (int32_t)job_meta[i] : -1;
     j.score_row = (rotate && scores) ? (int32_t)job_score_row[i] : -1;
+    if (rotate && metas[j.meta].rotate) {
+      const LayerDev& L = layers[j.layer];
+      const MetaDev& m = metas[j.meta];
+      const int64_t ntok = (int64_t)j.n_sel * L.page_size;
+      const int64_t len = std::min(m.len, ntok);
+      // positions must lie inside the table (index_select would raise)
+      const bool ok = mode == DARIC_ROPE_FLEXIBLE
+                          ? (m.pos_a >= 0 && m.pos_b >= 0 && m.pos_a + len <= L.max_pos && m.pos_b + len <= L.max_pos)
+                          : (m.pos_a >= 0 && m.pos_a < L.max_pos);
+      DARIC_CHECK(len <= 0 || ok, "rotary position out of range of cos_sin_cache (max_position=" +
+                                      std::to_string(L.max_pos) + ") at chunk " + std::to_string(j.meta));
+      auto key2 = std::make_pair((int64_t)j.meta, (const void*)L.table);
+      auto it = run_of.find(key2);
+      if (it == run_of.end()) {
+        FacJobDev f{};
+        f.table = L.table;
+        f.table_row = L.table_row;
+        f.pos_a = m.pos_a;
+        f.pos_b = m.pos_b;
+        f.len = len;
+        f.half_rot = L.half_rot;
+        f.P = L.pair_vecs;
+        it = run_of.emplace(key2, runs.size()).first;
+        runs.push_back(f);
+        run_tokens.push_back(ntok);
+      } else {
+        DARIC_CHECK(runs[it->second].half_rot == L.half_rot && runs[it->second].P == L.pair_vecs,
+                    "layers sharing a rotary table must share its rotary_dim");
+        runs[it->second].len = std::max(runs[it->second].len, len);
+        run_tokens[it->second] = std::max(run_tokens[it->second], ntok);
+      }
+    }
     jobs.push_back(j);
     units += jp.n_sel[i];
   }
   if (units == 0) return;
+  // token offsets and float4 item offsets of the runs
+  // runs of different rotary_dim use different token strides: each run
+  // starts at the first token of its own stride past the previous run
+  int64_t items = 0, fac_bytes = 0;
+  for (size_t r = 0; r < runs.size(); ++r) {
+    const int64_t tok_bytes = (int64_t)runs[r].half_rot * 8;
+    runs[r].out_tok = (fac_bytes + tok_bytes - 1) / tok_bytes;
+    runs[r].item_begin = items;
+    items += runs[r].len * (runs[r].half_rot / 2);
+    fac_bytes = (runs[r].out_tok + run_tokens[r]) * tok_bytes;
+  }
+  for (auto& j : jobs)
+    if (j.meta >= 0 && metas[j.meta].rotate)
+      j.fac_tok = runs[run_of[std::make_pair((int64_t)j.meta, (const void*)layers[j.layer].table)]].out_tok;
+  runs.erase(std::remove_if(runs.begin(), runs.end(), [](const FacJobDev& f) { return f.len <= 0; }), runs.end());
   DeviceGuard dg(jp.device);
   Blob b;
   const size_t o_layers = b.add(layers.size() * sizeof(LayerDev));
   const size_t o_jobs = b.add(jobs.size() * sizeof(JobDev));
   const size_t o_metas = b.add(metas.size() * sizeof(MetaDev));
+  const size_t o_runs = b.add(runs.size() * sizeof(FacJobDev));
   Upload up(dc, b.size);
   std::memcpy(up.host() + o_layers, layers.data(), layers.size() * sizeof(LayerDev));
   std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
   if (!metas.empty()) std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
+  if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
+  float4* fac = fac_bytes > 0 ? reinterpret_cast<float4*>(up.scratch((size_t)fac_bytes)) : nullptr;
   up.send(b.size, stream);
+  if (!runs.empty()) {
+    FactorLaunch fl{};
+    fl.jobs = reinterpret_cast<const FacJobDev*>(up.dev() + o_runs);
+    fl.num_jobs = (int64_t)runs.size();
+    fl.total_items = items;
+    fl.out = fac;
+    fl.mode = mode;
+    fl.fpv = factors_per_task(key.kv_dtype, key.neox != 0);
+    launch_factors(fl, key.tab_dtype, dc.sm_count, stream);
+  }
   PageLaunch p{};
   p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_layers);
   p.jobs = reinterpret_cast<const JobDev*>(up.dev() + o_jobs);
@@ -454,9 +543,9 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   p.scores = scores;
   p.score_ld = score_ld;
   p.err = dc.err_word;
-  p.smem_bytes = 0;
-  for (const auto& l : layers) p.smem_bytes = std::max(p.smem_bytes, rotate_smem_bytes(l.page_size, l.half_rot));
-  const BulkGeom bg = (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate) : BulkGeom{};
+  p.fac = fac;
+  const BulkGeom bg =
+      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate, rotate && scores) : BulkGeom{};
   if (bg.nstage >= 2) {
     if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
     else launch_bulk_plain(p, bg, gather, dc.sm_count, stream);
@@ -532,8 +621,7 @@ void resolve_rotary(LayerHost& L, int kv_dtype, const void* table, int tab_dtype
   DARIC_CHECK(rot_dim > 0 && rot_dim % 2 == 0 && rot_dim <= head_dim,
               "rotary_dim must be positive, even, and no greater than the K head dimension");
   DARIC_CHECK(page_size >= 1 && page_size <= 1024, "rerotate: block size must be in [1, 1024]");
-  DARIC_CHECK(rotate_smem_bytes((int)page_size, (int)(rot_dim / 2)) <= 200 * 1024,
-              "rerotate: block_size * rotary_dim too large for the shared-memory factor table");
+
   const int64_t half = rot_dim / 2;
   const int64_t row_bytes = row_elems * kv_es;
   DARIC_CHECK(row_bytes % 16 == 0, "rerotate: K row bytes must be a multiple of 16");
@@ -743,67 +831,114 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
     DARIC_CHECK(names && seg_blk_off && seg_tok_start && seg_tok_len && seg_pos_a, "segment arrays are NULL");
     DARIC_CHECK(mode != DARIC_ROPE_FLEXIBLE || seg_pos_b, "FLEXIBLE mode needs seg_pos_b");
     DARIC_CHECK(block_table != nullptr, "block_table is NULL");
-    std::vector<LayerHost*> layers(num_layers);
+    std::vector<LayerHost*> all(num_layers);
     for (int64_t l = 0; l < num_layers; ++l) {
-      layers[l] = &find_layer(c, names[l]);
-      DARIC_CHECK(layers[l]->has_rot, "layer has no rotary table (register_rotary): " + layers[l]->name);
+      all[l] = &find_layer(c, names[l]);
+      DARIC_CHECK(all[l]->has_rot, "layer has no rotary table (register_rotary): " + all[l]->name);
     }
-    const LayerHost& L0 = *layers[0];
-    for (auto* L : layers) {
+    const LayerHost& L0 = *all[0];
+    for (auto* L : all) {
       DARIC_CHECK(L->device == L0.device, "all layers must be on the same device");
-      DARIC_CHECK(L->kv_dtype == L0.kv_dtype && L->tab_dtype == L0.tab_dtype && L->neox == L0.neox &&
-                      L->dev.page_size == L0.dev.page_size,
-                  "rerotate_inplace: layers of one call must share dtype, table dtype, style and block size");
+      DARIC_CHECK(L->kv_dtype == L0.kv_dtype && L->neox == L0.neox && L->dev.page_size == L0.dev.page_size,
+                  "rerotate_inplace: layers of one call must share dtype, rotary style and block size");
+    }
+    // one launch per rotary table (the factors of a token depend on the table)
+    std::vector<std::vector<LayerHost*>> by_table;
+    for (auto* L : all) {
+      bool placed = false;
+      for (auto& grp : by_table)
+        if (grp[0]->dev.table == L->dev.table && grp[0]->dev.half_rot == L->dev.half_rot &&
+            grp[0]->tab_dtype == L->tab_dtype) {
+          grp.push_back(L);
+          placed = true;
+          break;
+        }
+      if (!placed) by_table.push_back({L});
     }
     const int64_t bs = L0.dev.page_size;
-    std::vector<SegDev> segs;
-    segs.reserve(num_segs);
-    int64_t units = 0;
-    for (int64_t s = 0; s < num_segs; ++s) {
-      DARIC_CHECK(seg_tok_len[s] >= 0 && seg_tok_start[s] >= 0 && seg_blk_off[s] >= 0,
-                  "negative segment field at segment " + std::to_string(s));
-      if (seg_tok_len[s] == 0) continue;
-      SegDev d{};
-      d.blk_off = seg_blk_off[s];
-      d.tok_start = seg_tok_start[s];
-      d.tok_len = seg_tok_len[s];
-      d.pos_a = seg_pos_a[s];
-      d.pos_b = mode == DARIC_ROPE_FLEXIBLE ? seg_pos_b[s] : 0;
-      const int64_t p0 = d.tok_start / bs, p1 = (d.tok_start + d.tok_len - 1) / bs;
-      DARIC_CHECK(d.blk_off + p1 < block_table_numel,
-                  "segment " + std::to_string(s) + " reaches past the block table");
-      d.first_page = (int32_t)p0;
-      d.num_units = (int32_t)(p1 - p0 + 1);
-      d.unit_begin = units;
-      units += d.num_units;
-      segs.push_back(d);
-    }
-    if (units == 0) return;
     DeviceCtx& dc = device_ctx(L0.device);
     DeviceGuard dg(L0.device);
-    std::vector<LayerDev> ld(num_layers);
-    for (int64_t l = 0; l < num_layers; ++l) ld[l] = base_layer_dev(*layers[l]);
-    Blob b;
-    const size_t o_l = b.add(ld.size() * sizeof(LayerDev));
-    const size_t o_s = b.add(segs.size() * sizeof(SegDev));
-    Upload up(dc, b.size);
-    std::memcpy(up.host() + o_l, ld.data(), ld.size() * sizeof(LayerDev));
-    std::memcpy(up.host() + o_s, segs.data(), segs.size() * sizeof(SegDev));
-    up.send(b.size, (cudaStream_t)stream);
-    InplaceLaunch p{};
-    p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_l);
-    p.num_layers = num_layers;
-    p.segs = reinterpret_cast<const SegDev*>(up.dev() + o_s);
-    p.num_segs = (int64_t)segs.size();
-    p.units_per_layer = units;
-    p.block_table = block_table;
-    p.block_table_numel = block_table_numel;
-    p.mode = mode;
-    p.err = dc.err_word;
-    p.smem_bytes = 0;
-    for (const auto& l : ld) p.smem_bytes = std::max(p.smem_bytes, rotate_smem_bytes(l.page_size, l.half_rot));
-    launch_rotate_inplace(p, RotKey{L0.kv_dtype, L0.tab_dtype, L0.neox}, dc.sm_count, (cudaStream_t)stream);
-    up.finish((cudaStream_t)stream);
+    for (auto& grp : by_table) {
+      const LayerDev& T0 = grp[0]->dev;
+      std::vector<SegDev> segs;
+      std::vector<FacJobDev> runs;
+      segs.reserve(num_segs);
+      int64_t units = 0, tok = 0, items = 0;
+      for (int64_t s = 0; s < num_segs; ++s) {
+        DARIC_CHECK(seg_tok_len[s] >= 0 && seg_tok_start[s] >= 0 && seg_blk_off[s] >= 0,
+                    "negative segment field at segment " + std::to_string(s));
+        if (seg_tok_len[s] == 0) continue;
+        SegDev d{};
+        d.blk_off = seg_blk_off[s];
+        d.tok_start = seg_tok_start[s];
+        d.tok_len = seg_tok_len[s];
+        d.pos_a = seg_pos_a[s];
+        d.pos_b = mode == DARIC_ROPE_FLEXIBLE ? seg_pos_b[s] : 0;
+        const bool ok = mode == DARIC_ROPE_FLEXIBLE
+                            ? (d.pos_a >= 0 && d.pos_b >= 0 && d.pos_a + d.tok_len <= T0.max_pos &&
+                               d.pos_b + d.tok_len <= T0.max_pos)
+                            : (d.pos_a >= 0 && d.pos_a < T0.max_pos);
+        DARIC_CHECK(ok, "rotary position out of range of cos_sin_cache (max_position=" +
+                            std::to_string(T0.max_pos) + ") at segment " + std::to_string(s));
+        const int64_t p0 = d.tok_start / bs, p1 = (d.tok_start + d.tok_len - 1) / bs;
+        DARIC_CHECK(d.blk_off + p1 < block_table_numel,
+                    "segment " + std::to_string(s) + " reaches past the block table");
+        d.first_page = (int32_t)p0;
+        d.num_units = (int32_t)(p1 - p0 + 1);
+        d.unit_begin = units;
+        d.fac_tok = tok;
+        units += d.num_units;
+        FacJobDev f{};
+        f.table = T0.table;
+        f.table_row = T0.table_row;
+        f.pos_a = d.pos_a;
+        f.pos_b = d.pos_b;
+        f.len = d.tok_len;
+        f.out_tok = tok;
+        f.item_begin = items;
+        f.half_rot = T0.half_rot;
+        f.P = T0.pair_vecs;
+        runs.push_back(f);
+        items += d.tok_len * (T0.half_rot / 2);
+        tok += d.tok_len;
+        segs.push_back(d);
+      }
+      if (units == 0) return;
+      std::vector<LayerDev> ld(grp.size());
+      for (size_t l = 0; l < grp.size(); ++l) ld[l] = base_layer_dev(*grp[l]);
+      Blob b;
+      const size_t o_l = b.add(ld.size() * sizeof(LayerDev));
+      const size_t o_s = b.add(segs.size() * sizeof(SegDev));
+      const size_t o_r = b.add(runs.size() * sizeof(FacJobDev));
+      Upload up(dc, b.size);
+      std::memcpy(up.host() + o_l, ld.data(), ld.size() * sizeof(LayerDev));
+      std::memcpy(up.host() + o_s, segs.data(), segs.size() * sizeof(SegDev));
+      std::memcpy(up.host() + o_r, runs.data(), runs.size() * sizeof(FacJobDev));
+      float4* fac = reinterpret_cast<float4*>(up.scratch((size_t)tok * T0.half_rot * 8));
+      up.send(b.size, (cudaStream_t)stream);
+      FactorLaunch fl{};
+      fl.jobs = reinterpret_cast<const FacJobDev*>(up.dev() + o_r);
+      fl.num_jobs = (int64_t)runs.size();
+      fl.total_items = items;
+      fl.out = fac;
+      fl.mode = mode;
+      fl.fpv = factors_per_task(L0.kv_dtype, L0.neox != 0);
+      launch_factors(fl, grp[0]->tab_dtype, dc.sm_count, (cudaStream_t)stream);
+      InplaceLaunch p{};
+      p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_l);
+      p.num_layers = (int64_t)grp.size();
+      p.segs = reinterpret_cast<const SegDev*>(up.dev() + o_s);
+      p.num_segs = (int64_t)segs.size();
+      p.units_per_layer = units;
+      p.block_table = block_table;
+      p.block_table_numel = block_table_numel;
+      p.mode = mode;
+      p.err = dc.err_word;
+      p.fac = fac;
+      launch_rotate_inplace(p, RotKey{L0.kv_dtype, grp[0]->tab_dtype, L0.neox}, dc.sm_count,
+                            (cudaStream_t)stream);
+      up.finish((cudaStream_t)stream);
+    }
   });
 }
 

@@ -97,19 +97,56 @@ __device__ __forceinline__ uint4 pack(const float (&in)[E::kPerVec]) {
   return v;
 }
 
+// Packs N fp32 values into one 16-byte vector of the element type, two at a
+// time with the paired round-to-nearest-even conversions (bit-identical to
+// converting each value on its own).
+template <class E>
+__device__ __forceinline__ uint4 pack_vec(const float (&in)[E::kPerVec]);
+
+template <>
+__device__ __forceinline__ uint4 pack_vec<Elem<DARIC_DTYPE_BF16>>(const float (&in)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ uint4 pack_vec<Elem<DARIC_DTYPE_F16>>(const float (&in)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(in[2 * i], in[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ uint4 pack_vec<Elem<DARIC_DTYPE_F32>>(const float (&in)[4]) {
+  return make_uint4(__float_as_uint(in[0]), __float_as_uint(in[1]), __float_as_uint(in[2]),
+                    __float_as_uint(in[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack_vec<Elem<DARIC_DTYPE_FP8_E4M3>>(const float (&in)[16]) {
+  return pack<Elem<DARIC_DTYPE_FP8_E4M3>>(in);
+}
+
 // cos/sin factor of one rotary frequency `d` (fp32 result).
 //   FLEXIBLE: C = n_c*o_c + n_s*o_s, S = n_s*o_c - n_c*o_s, every product and
 //             sum rounded to the table dtype (torch ops on the model-dtype
 //             table, adapter.py:276-283).
 //   DELTA   : C, S = table row `pa` (adapter.py:181-183).
 template <class T>
-__device__ __forceinline__ float2 rope_factor(const LayerDev& L, int mode, int64_t pa, int64_t pb, int d) {
+__device__ __forceinline__ float2 rope_factor(const uint8_t* table, int64_t table_row, int half_rot, int mode,
+                                              int64_t pa, int64_t pb, int d) {
   using R = typename T::raw;
-  const R* orow = reinterpret_cast<const R*>(L.table + pa * L.table_row);
-  if (mode == DARIC_ROPE_DELTA) return make_float2(T::to_f(orow[d]), T::to_f(orow[L.half_rot + d]));
-  const R* nrow = reinterpret_cast<const R*>(L.table + pb * L.table_row);
-  const float oc = T::to_f(orow[d]), os = T::to_f(orow[L.half_rot + d]);
-  const float nc = T::to_f(nrow[d]), ns = T::to_f(nrow[L.half_rot + d]);
+  const R* orow = reinterpret_cast<const R*>(table + pa * table_row);
+  if (mode == DARIC_ROPE_DELTA) return make_float2(T::to_f(orow[d]), T::to_f(orow[half_rot + d]));
+  const R* nrow = reinterpret_cast<const R*>(table + pb * table_row);
+  const float oc = T::to_f(orow[d]), os = T::to_f(orow[half_rot + d]);
+  const float nc = T::to_f(nrow[d]), ns = T::to_f(nrow[half_rot + d]);
   const float a = T::round_f(__fmul_rn(nc, oc));
   const float b = T::round_f(__fmul_rn(ns, os));
   const float c = T::round_f(__fmul_rn(ns, oc));
@@ -117,102 +154,84 @@ __device__ __forceinline__ float2 rope_factor(const LayerDev& L, int mode, int64
   return make_float2(T::round_f(__fadd_rn(a, b)), T::round_f(__fsub_rn(c, e)));
 }
 
-// Shared-memory layout of a page's rotation state:
-//   fac[page_size*half_rot] float2 factors, ok[page_size] int flags,
-//   dev[page_size] float deviations.
-struct PageSmem {
-  float2* fac;
-  int* ok;
-  float* dev;
-};
+// Factor layout of one token (written by the factor pre-pass): the rotation
+// task c of a row (c < P = half_rot / FPV) uses FPV consecutive frequencies
+// d = c*FPV + j; they are stored as FPV/2 float4 groups
+//   q[g*P + c] = {C[d0], C[d0+1], S[d0], S[d0+1]},  d0 = c*FPV + 2g,
+// so the 32 lanes of a warp (consecutive c) read consecutive 16-byte words.
+// FPV = elements per 16-byte vector (NeoX) or half of it (GPT-J).
 
-__device__ __forceinline__ PageSmem page_smem(void* base, const LayerDev& L) {
-  PageSmem s;
-  s.fac = reinterpret_cast<float2*>(base);
-  s.ok = reinterpret_cast<int*>(s.fac + L.page_size * L.half_rot);
-  s.dev = reinterpret_cast<float*>(s.ok + L.page_size);
-  return s;
-}
-
-// Fills the factors of the page slots s whose token t = tok0 + s lies in
-// [0, len): positions (a + t, b + t) in FLEXIBLE mode, a in DELTA mode.
-// ok[s] = 0 marks slots that are not rotated (outside the range, or a
-// position outside the table, which also sets the device error bit).
-template <class T>
-__device__ __forceinline__ void fill_factors(const LayerDev& L, int mode, int64_t pa, int64_t pb,
-                                             int64_t tok0, int64_t len, PageSmem sm, int* err) {
-  for (int s = threadIdx.x; s < L.page_size; s += blockDim.x) {
-    const int64_t t = tok0 + s;
-    int ok = 0;
-    if (t >= 0 && t < len) {
-      int64_t a = pa, b = pb;
-      if (mode == DARIC_ROPE_FLEXIBLE) { a += t; b += t; }
-      ok = a >= 0 && a < L.max_pos && (mode != DARIC_ROPE_FLEXIBLE || (b >= 0 && b < L.max_pos));
-      if (!ok) atomicOr(err, DEV_ERR_TABLE_RANGE);
-    }
-    sm.ok[s] = ok;
-  }
-  __syncthreads();
-  const int n = L.page_size * L.half_rot;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int s = i / L.half_rot, d = i - s * L.half_rot;
-    if (!sm.ok[s]) continue;
-    const int64_t t = tok0 + s;
-    int64_t a = pa, b = pb;
-    if (mode == DARIC_ROPE_FLEXIBLE) { a += t; b += t; }
-    sm.fac[i] = rope_factor<T>(L, mode, a, b, d);
-  }
-}
-
-// Rotates one NeoX pair of vectors (x1 = elements d0.., x2 = d0+half..):
-//   x1' = x1*C - x2*S ; x2' = x2*C + x1*S   (fp32, no contraction)
-// and accumulates the squared change of the stored values into `dev`.
-template <class E>
-__device__ __forceinline__ void rotate_neox(const float2* f, uint4& lo, uint4& hi, float& dev) {
+// x1' = x1*C - x2*S ; x2' = x2*C + x1*S on NeoX halves, in fp32 with paired
+// multiplies and adds (no contraction), rounded back to the element type.
+template <class E, bool SCORE>
+__device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo, uint4& hi, float& dev) {
   constexpr int N = E::kPerVec;
   float k1[N], k2[N], o1[N], o2[N];
   unpack<E>(lo, k1);
   unpack<E>(hi, k2);
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    const float2 cs = f[i];
-    o1[i] = __fsub_rn(__fmul_rn(k1[i], cs.x), __fmul_rn(k2[i], cs.y));
-    o2[i] = __fadd_rn(__fmul_rn(k2[i], cs.x), __fmul_rn(k1[i], cs.y));
+  for (int g = 0; g < N / 2; ++g) {
+    const float4 f = q[g * P];
+    const float2 c2 = make_float2(f.x, f.y), s2 = make_float2(f.z, f.w);
+    const float2 ns2 = make_float2(-f.z, -f.w);
+    const float2 a = make_float2(k1[2 * g], k1[2 * g + 1]);
+    const float2 b = make_float2(k2[2 * g], k2[2 * g + 1]);
+    const float2 r1 = __fadd2_rn(__fmul2_rn(a, c2), __fmul2_rn(b, ns2));
+    const float2 r2 = __fadd2_rn(__fmul2_rn(b, c2), __fmul2_rn(a, s2));
+    o1[2 * g] = r1.x; o1[2 * g + 1] = r1.y;
+    o2[2 * g] = r2.x; o2[2 * g + 1] = r2.y;
   }
-  lo = pack<E>(o1);
-  hi = pack<E>(o2);
-  float r1[N], r2[N];
-  unpack<E>(lo, r1);
-  unpack<E>(hi, r2);
+  lo = pack_vec<E>(o1);
+  hi = pack_vec<E>(o2);
+  if (SCORE) {
+    float r1[N], r2[N];
+    unpack<E>(lo, r1);
+    unpack<E>(hi, r2);
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    const float a = r1[i] - k1[i];
-    const float b = r2[i] - k2[i];
-    dev += a * a + b * b;
+    for (int i = 0; i < N; ++i) {
+      const float a = r1[i] - k1[i];
+      const float b = r2[i] - k2[i];
+      dev += a * a + b * b;
+    }
   }
 }
 
-// Rotates one GPT-J vector: adjacent pairs (2m, 2m+1) with factor f[m].
-template <class E>
-__device__ __forceinline__ void rotate_gptj(const float2* f, uint4& v, float& dev) {
+// GPT-J: adjacent pairs (2m, 2m+1) of one vector rotate with frequency
+// c*FPV + m.
+template <class E, bool SCORE>
+__device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, float& dev) {
   constexpr int N = E::kPerVec;
   float k[N], o[N];
   unpack<E>(v, k);
 #pragma unroll
-  for (int m = 0; m < N / 2; ++m) {
-    const float2 cs = f[m];
-    const float x1 = k[2 * m], x2 = k[2 * m + 1];
-    o[2 * m] = __fsub_rn(__fmul_rn(x1, cs.x), __fmul_rn(x2, cs.y));
-    o[2 * m + 1] = __fadd_rn(__fmul_rn(x2, cs.x), __fmul_rn(x1, cs.y));
-  }
-  v = pack<E>(o);
-  float r[N];
-  unpack<E>(v, r);
+  for (int g = 0; g < N / 4; ++g) {
+    const float4 f = q[g * P];
 #pragma unroll
-  for (int i = 0; i < N; ++i) {
-    const float a = r[i] - k[i];
-    dev += a * a;
+    for (int e = 0; e < 2; ++e) {
+      const float c = e ? f.y : f.x, s = e ? f.w : f.z;
+      const float2 a = make_float2(k[4 * g + 2 * e], k[4 * g + 2 * e + 1]);  // (x_even, x_odd)
+      const float2 b = make_float2(a.y, a.x);
+      const float2 r = __fadd2_rn(__fmul2_rn(a, make_float2(c, c)), __fmul2_rn(b, make_float2(-s, s)));
+      o[4 * g + 2 * e] = r.x;
+      o[4 * g + 2 * e + 1] = r.y;
+    }
   }
+  v = pack_vec<E>(o);
+  if (SCORE) {
+    float r[N];
+    unpack<E>(v, r);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const float a = r[i] - k[i];
+      dev += a * a;
+    }
+  }
+}
+
+// Token slot of K row `row` of a page region.
+__device__ __forceinline__ int row_slot(const LayerDev& L, int row) {
+  const uint32_t q = fdiv((uint32_t)row, L.tok_div);
+  return (int)(q - fdiv(q, L.tok_mod) * (uint32_t)L.page_size);
 }
 
 }  // namespace dev

@@ -101,6 +101,7 @@ struct JobDev {
   int64_t stg_off;     // byte offset into the store buffer
   int64_t idx_off;     // first entry of this job's block ids in indices_flat
   int64_t unit_begin;  // first unit (page) of this job within the launch
+  int64_t fac_tok;     // factor-buffer token of the chunk's token 0 (its table)
   int32_t n_sel;       // pages of this job
   int32_t layer;       // index into the launch's LayerDev table
   int32_t meta;        // chunk index (-1 = none)
@@ -130,7 +131,7 @@ struct PageLaunch {
   float* scores;
   int64_t score_ld;
   int* err;                  // device error word
-  size_t smem_bytes;         // dynamic shared memory of the rotating kernel
+  const float4* fac;         // rotary factors (factor pre-pass output)
 };
 
 // In-place rotation segments.
@@ -140,6 +141,7 @@ struct SegDev {
   int64_t tok_len;     // tokens
   int64_t pos_a, pos_b;
   int64_t unit_begin;  // first unit (page-slice) of the segment
+  int64_t fac_tok;     // factor-buffer token of the segment's token 0
   int32_t first_page;  // tok_start / page_size
   int32_t num_units;   // pages touched
 };
@@ -154,14 +156,33 @@ struct InplaceLaunch {
   int64_t block_table_numel;
   int32_t mode;
   int* err;
-  size_t smem_bytes;
+  const float4* fac;
 };
 
-// Dynamic shared memory of the rotating kernels for one layer geometry:
-// factors (float2 per slot and frequency), slot flags and deviations.
-inline size_t rotate_smem_bytes(int page_size, int half_rot) {
-  return (size_t)page_size * half_rot * 8 + (size_t)page_size * 8;
-}
+// Factor pre-pass: one run of tokens [0, len) of a chunk (or segment) with
+// one rotary table, written at factor-buffer token out_tok.
+struct FacJobDev {
+  const uint8_t* table;
+  int64_t table_row;   // bytes per table row
+  int64_t pos_a, pos_b;
+  int64_t len;
+  int64_t out_tok;
+  int64_t item_begin;  // first float4 of this run within the launch
+  int32_t half_rot;
+  int32_t P;           // rotation tasks per row (half_rot / fpv)
+};
+
+struct FactorLaunch {
+  const FacJobDev* jobs;
+  int64_t num_jobs;
+  int64_t total_items;  // float4 count
+  float4* out;
+  int32_t mode;
+  int32_t fpv;          // factors per rotation task
+};
+
+// Factor-block bytes of one page: page_size tokens x half_rot float2.
+__host__ __device__ inline size_t page_factor_bytes(int page_size, int half_rot) { return (size_t)page_size * half_rot * 8; }
 
 struct SelSegDev {
   int64_t col_off, len, pos0, k, blk_off, out_off;
@@ -207,16 +228,17 @@ enum : int {
 };
 
 // Geometry of the bulk-copy pipeline: NSTAGE shared-memory stages of
-// stage_bytes each, after a fac_bytes rotation-state region.
+// stage_bytes each (page data, then fac_off.. the page's factor block),
+// after a dev_bytes region of per-slot deviations.
 struct BulkGeom {
   int32_t nstage;
   int32_t stage_bytes;
-  int32_t fac_bytes;
-  int32_t pad;
+  int32_t fac_off;    // offset of the factor block inside a stage
+  int32_t dev_bytes;
 };
 
 inline size_t bulk_smem_bytes(const BulkGeom& g) {
-  return 256 + (size_t)g.fac_bytes + (size_t)g.nstage * g.stage_bytes;
+  return 256 + (size_t)g.dev_bytes + (size_t)g.nstage * g.stage_bytes;
 }
 
 // ------------------------------------------------------------ launchers --
@@ -226,6 +248,7 @@ struct RotKey {
 };
 
 void launch_plain_pages(const PageLaunch& p, bool gather, bool vec16, int sm_count, cudaStream_t s);
+void launch_factors(const FactorLaunch& p, int tab_dtype, int sm_count, cudaStream_t s);
 void launch_rotate_scatter(const PageLaunch& p, RotKey key, int sm_count, cudaStream_t s);
 void launch_rotate_inplace(const InplaceLaunch& p, RotKey key, int sm_count, cudaStream_t s);
 void launch_bulk_plain(const PageLaunch& p, const BulkGeom& g, bool gather, int sm_count, cudaStream_t s);
