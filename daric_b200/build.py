@@ -30,9 +30,12 @@ def nvcc() -> str:
 
 
 def _flags() -> list[str]:
+    # -fmad=false: the rotation is specified as separately rounded products
+    # and sums (the reference's math without contraction); no mul+add pair
+    # may be fused into an FMA.
     return [
-        "-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-        "-I", str(ROOT / "include"), "-DNDEBUG",
+        "-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler",
+        "-fvisibility=hidden", "-I", str(ROOT / "include"), "-DNDEBUG",
     ]
 
 

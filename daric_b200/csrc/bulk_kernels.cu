@@ -12,8 +12,8 @@
 // Every wait is bounded: an mbarrier wait that exceeds kWaitLimit rounds
 // sets DEV_ERR_TIMEOUT, drains the copies this CTA has in flight (again with
 // a bound) and returns.
+#include <map>
 #include <mutex>
-#include <unordered_map>
 
 #include "device_common.cuh"
 #include "internal.h"
@@ -274,13 +274,16 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
 template <class K>
 void launch_bulk(K kernel, const PageLaunch& p, const BulkGeom& g, int sm_count, cudaStream_t s) {
   static std::mutex mu;
-  static std::unordered_map<const void*, size_t> attr;
+  static std::map<std::pair<const void*, int>, size_t> attr;  // (kernel, device) -> smem set
   const size_t smem = bulk_smem_bytes(g);
   {
+    int dev = 0;
+    DARIC_CUDA(cudaGetDevice(&dev));
     std::lock_guard<std::mutex> lk(mu);
-    if (attr[(const void*)kernel] < smem) {
+    size_t& cur = attr[std::make_pair((const void*)kernel, dev)];
+    if (cur < smem) {
       DARIC_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      attr[(const void*)kernel] = smem;
+      cur = smem;
     }
   }
   const int grid = (int)(p.total_units < sm_count ? p.total_units : sm_count);

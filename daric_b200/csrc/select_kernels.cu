@@ -9,6 +9,9 @@
 //    (daric/adaption/policy.py:45-103) into positions and slots, the slot
 //    formula of the recompute sub-requests (integration/vllm/worker.py:310-346):
 //    slot = block_ids[p // bs] * bs + p % bs.
+#include <mutex>
+#include <set>
+
 #include "internal.h"
 
 namespace daric {
@@ -51,10 +54,19 @@ __device__ __forceinline__ int block_scan(int v, int* total, int* sm) {
   return x - v + (warp > 0 ? sm[warp - 1] : 0);
 }
 
+// Rows of up to kSmemKeys keys are staged in shared memory (one read of the
+// scores); longer rows are re-read from global memory (L2) on every pass.
+constexpr int kSmemKeys = 12288;
+
+__device__ __forceinline__ uint32_t key_at(const float* row, const uint32_t* skeys, bool staged, int64_t i) {
+  return staged ? skeys[i] : score_key(row[i]);
+}
+
 __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
   __shared__ uint32_t hist[256];
   __shared__ int scan_sm[32];
   __shared__ uint32_t s_digit, s_above;
+  extern __shared__ uint32_t skeys[];
 
   const int64_t si = blockIdx.x, l = blockIdx.y;
   const SelSegDev sg = p.segs[si];
@@ -63,6 +75,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
   int32_t* oidx = p.out_idx + l * p.out_ld + sg.out_off;
   int64_t* oslot = p.out_slot + l * p.out_ld + sg.out_off;
   const bool topk = p.mode == DARIC_SELECT_TOPK;
+  const bool staged = n <= kSmemKeys;
 
   uint32_t thr = 0;     // k-th largest key (top-k)
   int64_t take_eq = 0;  // keys equal to thr that are taken, lowest index first
@@ -73,22 +86,29 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
       if (threadIdx.x == 0) p.out_count[l * p.num_segs + si] = 0;
       return;
     }
-    if (k == n) {
-      take_all = true;
-    } else {
+    take_all = (k == n);
+    if (!take_all) {
+      if (staged) {
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) skeys[i] = score_key(__ldg(&row[i]));
+      }
       uint32_t prefix = 0, mask = 0;
       int64_t rem = k;
+      const int lane = threadIdx.x & 31;
       for (int shift = 24; shift >= 0; shift -= 8) {
         for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
         __syncthreads();
-        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-          const uint32_t key = score_key(row[i]);
-          if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        for (int64_t i = threadIdx.x; i - threadIdx.x < n; i += blockDim.x) {
+          const bool in = i < n;
+          const uint32_t key = in ? key_at(row, skeys, staged, i) : 0u;
+          const bool act = in && (key & mask) == prefix;
+          const uint32_t digit = act ? ((key >> shift) & 255u) : 256u + lane;
+          // lanes with the same digit add once (warp-aggregated atomics)
+          const uint32_t peers = __match_any_sync(0xffffffffu, digit);
+          if (act && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
         }
         __syncthreads();
         if (threadIdx.x < 32) {
           // lane L owns digits [248-8L, 255-8L], scanned from the top.
-          const int lane = threadIdx.x;
           uint32_t cnt[8], sum = 0;
 #pragma unroll
           for (int q = 0; q < 8; ++q) { cnt[q] = hist[255 - 8 * lane - q]; sum += cnt[q]; }
@@ -122,42 +142,74 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
     }
   }
 
+  // Compaction in token order: warp w owns the 512 consecutive keys
+  // [c0 + 512w, c0 + 512(w+1)) of each pass, as 16 rounds of 32 (lane = key),
+  // so ballots give in-warp ranks and one block scan orders the warps.
+  const bool use_keys = topk && !take_all;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  constexpr int R = 16;
+  const int64_t span = (int64_t)kSelWarps * 32 * R;
   int64_t running = 0, eq_seen = 0;
-  for (int64_t c0 = 0; c0 < n; c0 += blockDim.x) {
-    const int64_t i = c0 + threadIdx.x;
-    bool sel = false, eq = false;
-    if (i < n) {
-      const float f = row[i];
-      if (!topk) {
-        sel = f >= p.threshold;
-      } else if (take_all) {
-        sel = true;
-      } else {
-        const uint32_t key = score_key(f);
-        sel = key > thr;
-        eq = key == thr;
+  for (int64_t c0 = 0; c0 < n; c0 += span) {
+    const int64_t wb = c0 + (int64_t)warp * 32 * R;
+    uint32_t selm[R], eqm[R];
+    int sel_cnt = 0, eq_cnt = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t i = wb + r * 32 + lane;
+      bool sel = false, eq = false;
+      if (i < n) {
+        if (!topk) {
+          sel = row[i] >= p.threshold;
+        } else if (take_all) {
+          sel = true;
+        } else {
+          const uint32_t key = key_at(row, skeys, staged, i);
+          sel = key > thr;
+          eq = key == thr;
+        }
       }
+      selm[r] = __ballot_sync(0xffffffffu, sel);
+      eqm[r] = __ballot_sync(0xffffffffu, eq);
+      sel_cnt += __popc(selm[r]);
+      eq_cnt += __popc(eqm[r]);
     }
-    if (topk && !take_all) {
+    if (use_keys) {
       int eq_tot;
-      const int eq_rank = block_scan(eq ? 1 : 0, &eq_tot, scan_sm);
-      if (eq && eq_seen + eq_rank < take_eq) sel = true;
+      const int eq_off = __shfl_sync(0xffffffffu, block_scan(lane == 0 ? eq_cnt : 0, &eq_tot, scan_sm), 0);
+      // the lowest-index keys equal to thr are taken
+      int64_t rank = eq_seen + eq_off;
+      sel_cnt = 0;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const bool mine = (eqm[r] >> lane) & 1u;
+        const bool take = mine && rank + __popc(eqm[r] & lt_mask) < take_eq;
+        selm[r] |= __ballot_sync(0xffffffffu, take);
+        rank += __popc(eqm[r]);
+        sel_cnt += __popc(selm[r]);
+      }
       eq_seen += eq_tot;
     }
     int sel_tot;
-    const int rank = block_scan(sel ? 1 : 0, &sel_tot, scan_sm);
-    if (sel) {
-      const int64_t o = running + rank;
-      const int64_t pos = sg.pos0 + i;
-      const int64_t bt = sg.blk_off + pos / p.block_size;
-      int64_t slot = -1;
-      if (bt >= 0 && bt < p.block_table_numel) {
-        slot = (int64_t)__ldg(&p.block_table[bt]) * p.block_size + pos % p.block_size;
-      } else {
-        atomicOr(p.err, DEV_ERR_INDEX_RANGE);
+    int64_t o = running + __shfl_sync(0xffffffffu, block_scan(lane == 0 ? sel_cnt : 0, &sel_tot, scan_sm), 0);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if ((selm[r] >> lane) & 1u) {
+        const int64_t i = wb + r * 32 + lane;
+        const int64_t at = o + __popc(selm[r] & lt_mask);
+        const int64_t pos = sg.pos0 + i;
+        const int64_t bt = sg.blk_off + pos / p.block_size;
+        int64_t slot = -1;
+        if (bt >= 0 && bt < p.block_table_numel) {
+          slot = (int64_t)__ldg(&p.block_table[bt]) * p.block_size + pos % p.block_size;
+        } else {
+          atomicOr(p.err, DEV_ERR_INDEX_RANGE);
+        }
+        oidx[at] = (int32_t)pos;
+        oslot[at] = slot;
       }
-      oidx[o] = (int32_t)pos;
-      oslot[o] = slot;
+      o += __popc(selm[r]);
     }
     running += sel_tot;
   }
@@ -192,7 +244,19 @@ void launch_score_select(const SelectLaunch& p, cudaStream_t s) {
   if (p.num_segs <= 0 || p.num_layers <= 0) return;
   DARIC_CHECK(p.num_layers <= 65535, "score_select: at most 65535 layers per call");
   const dim3 grid((unsigned)p.num_segs, (unsigned)p.num_layers, 1);
-  select_kernel<<<grid, kSelThreads, 0, s>>>(p);
+  {
+    static std::mutex mu;
+    static std::set<int> done;  // devices whose function attribute is set
+    int dev = 0;
+    DARIC_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> g(mu);
+    if (!done.count(dev)) {
+      DARIC_CUDA(cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kSmemKeys * (int)sizeof(uint32_t)));
+      done.insert(dev);
+    }
+  }
+  select_kernel<<<grid, kSelThreads, kSmemKeys * sizeof(uint32_t), s>>>(p);
   DARIC_CUDA(cudaGetLastError());
 }
 
