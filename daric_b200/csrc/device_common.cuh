@@ -154,6 +154,25 @@ __device__ __forceinline__ float2 rope_factor(const uint8_t* table, int64_t tabl
   return make_float2(T::round_f(__fadd_rn(a, b)), T::round_f(__fsub_rn(c, e)));
 }
 
+// Paired fp32 multiply / add with explicit round-to-nearest: an explicit
+// rounding modifier keeps the compiler from fusing a multiply and an add into
+// one FMA, so every product and sum is rounded separately (bit-identical to
+// the scalar __fmul_rn / __fadd_rn sequence).
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&r);
+}
+
 // Factor layout of one token (written by the factor pre-pass): the rotation
 // task c of a row (c < P = half_rot / FPV) uses FPV consecutive frequencies
 // d = c*FPV + j; they are stored as FPV/2 float4 groups
@@ -176,8 +195,8 @@ __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo,
     const float2 ns2 = make_float2(-f.z, -f.w);
     const float2 a = make_float2(k1[2 * g], k1[2 * g + 1]);
     const float2 b = make_float2(k2[2 * g], k2[2 * g + 1]);
-    const float2 r1 = __fadd2_rn(__fmul2_rn(a, c2), __fmul2_rn(b, ns2));
-    const float2 r2 = __fadd2_rn(__fmul2_rn(b, c2), __fmul2_rn(a, s2));
+    const float2 r1 = add2_rn(mul2_rn(a, c2), mul2_rn(b, ns2));
+    const float2 r2 = add2_rn(mul2_rn(b, c2), mul2_rn(a, s2));
     o1[2 * g] = r1.x; o1[2 * g + 1] = r1.y;
     o2[2 * g] = r2.x; o2[2 * g + 1] = r2.y;
   }
@@ -211,7 +230,7 @@ __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, 
       const float c = e ? f.y : f.x, s = e ? f.w : f.z;
       const float2 a = make_float2(k[4 * g + 2 * e], k[4 * g + 2 * e + 1]);  // (x_even, x_odd)
       const float2 b = make_float2(a.y, a.x);
-      const float2 r = __fadd2_rn(__fmul2_rn(a, make_float2(c, c)), __fmul2_rn(b, make_float2(-s, s)));
+      const float2 r = add2_rn(mul2_rn(a, make_float2(c, c)), mul2_rn(b, make_float2(-s, s)));
       o[4 * g + 2 * e] = r.x;
       o[4 * g + 2 * e + 1] = r.y;
     }

@@ -88,8 +88,21 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
     }
     take_all = (k == n);
     if (!take_all) {
-      if (staged) {
-        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) skeys[i] = score_key(__ldg(&row[i]));
+      if (staged) {  // all loads of a batch in flight before any key is stored
+        constexpr int kBatch = 8;
+        for (int64_t b0 = threadIdx.x; b0 < n; b0 += (int64_t)kBatch * blockDim.x) {
+          float v[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int64_t i = b0 + (int64_t)u * blockDim.x;
+            v[u] = i < n ? __ldg(&row[i]) : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int64_t i = b0 + (int64_t)u * blockDim.x;
+            if (i < n) skeys[i] = score_key(v[u]);
+          }
+        }
       }
       uint32_t prefix = 0, mask = 0;
       int64_t rem = k;
