@@ -277,11 +277,13 @@ def run_ours(args):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         start.record(stream)
+        h0 = time.perf_counter()
         for i in range(args.steps):
             ev[i][0].record(stream)
             wl.load()
             ev[i][1].record(stream)
             wl.select()
+        host_us = (time.perf_counter() - h0) / args.steps * 1e6  # enqueue time per step
         end.record(stream)
         torch.cuda.synchronize()
     barrier()
@@ -362,7 +364,8 @@ def run_ours(args):
             "e2e": {"value": round(world * wl.bytes * e2e_steps / (e2e_ms_max * 1e-3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms_max / e2e_steps, 4)},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
+            "host_us_per_step": round(host_us, 1),
             "clocks": clk.summary(),
             "device_errors": errors,
         }

@@ -113,7 +113,13 @@ def i64(values) -> tuple[np.ndarray, C.POINTER(C.c_int64)]:
 
 
 def names_array(names) -> C.Array:
-    enc = [n.encode() if isinstance(n, str) else bytes(n) for n in names]
+    """char* array of layer names; an already-built array is passed through.
+    Repeated names share one encoded buffer (the library caches lookups by
+    pointer within a call)."""
+    if isinstance(names, C.Array):
+        return names
+    cache: dict[str, bytes] = {}
+    enc = [cache.setdefault(n, n.encode()) if isinstance(n, str) else bytes(n) for n in names]
     return (C.c_char_p * len(enc))(*enc)
 
 

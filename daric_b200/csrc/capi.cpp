@@ -346,11 +346,14 @@ JobPlan plan_jobs(daric_copier* c, int64_t num_jobs, const char* const* names, c
                 "store range out of bounds at job " + std::to_string(i));
   }
   std::unordered_map<LayerHost*, int> slot_of;
+  std::unordered_map<const char*, LayerHost*> by_ptr;  // callers repeat name buffers
   jp.layers.resize(num_jobs);
   jp.layer_slot.resize(num_jobs);
   jp.n_sel.resize(num_jobs);
   for (int64_t i = 0; i < num_jobs; ++i) {
-    LayerHost& L = find_layer(c, names[i]);
+    auto hit = by_ptr.find(names[i]);
+    if (hit == by_ptr.end()) hit = by_ptr.emplace(names[i], &find_layer(c, names[i])).first;
+    LayerHost& L = *hit->second;
     if (i == 0) jp.device = L.device;
     DARIC_CHECK(L.device == jp.device,
                 "all layers must be on the same device; job " + std::to_string(i));

@@ -154,25 +154,6 @@ __device__ __forceinline__ float2 rope_factor(const uint8_t* table, int64_t tabl
   return make_float2(T::round_f(__fadd_rn(a, b)), T::round_f(__fsub_rn(c, e)));
 }
 
-// Paired fp32 multiply / add with explicit round-to-nearest: an explicit
-// rounding modifier keeps the compiler from fusing a multiply and an add into
-// one FMA, so every product and sum is rounded separately (bit-identical to
-// the scalar __fmul_rn / __fadd_rn sequence).
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
-  return *reinterpret_cast<const float2*>(&r);
-}
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
-  return *reinterpret_cast<const float2*>(&r);
-}
-
 // Factor layout of one token (written by the factor pre-pass): the rotation
 // task c of a row (c < P = half_rot / FPV) uses FPV consecutive frequencies
 // d = c*FPV + j; they are stored as FPV/2 float4 groups
@@ -180,8 +161,9 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
 // so the 32 lanes of a warp (consecutive c) read consecutive 16-byte words.
 // FPV = elements per 16-byte vector (NeoX) or half of it (GPT-J).
 
-// x1' = x1*C - x2*S ; x2' = x2*C + x1*S on NeoX halves, in fp32 with paired
-// multiplies and adds (no contraction), rounded back to the element type.
+// x1' = x1*C - x2*S ; x2' = x2*C + x1*S on NeoX halves, in fp32 with every
+// product and sum rounded separately (__fmul_rn / __fadd_rn / __fsub_rn are
+// never fused into an FMA), rounded back to the element type.
 template <class E, bool SCORE>
 __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo, uint4& hi, float& dev) {
   constexpr int N = E::kPerVec;
@@ -191,14 +173,13 @@ __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo,
 #pragma unroll
   for (int g = 0; g < N / 2; ++g) {
     const float4 f = q[g * P];
-    const float2 c2 = make_float2(f.x, f.y), s2 = make_float2(f.z, f.w);
-    const float2 ns2 = make_float2(-f.z, -f.w);
-    const float2 a = make_float2(k1[2 * g], k1[2 * g + 1]);
-    const float2 b = make_float2(k2[2 * g], k2[2 * g + 1]);
-    const float2 r1 = add2_rn(mul2_rn(a, c2), mul2_rn(b, ns2));
-    const float2 r2 = add2_rn(mul2_rn(b, c2), mul2_rn(a, s2));
-    o1[2 * g] = r1.x; o1[2 * g + 1] = r1.y;
-    o2[2 * g] = r2.x; o2[2 * g + 1] = r2.y;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float c = e ? f.y : f.x, s = e ? f.w : f.z;
+      const float x1 = k1[2 * g + e], x2 = k2[2 * g + e];
+      o1[2 * g + e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      o2[2 * g + e] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    }
   }
   lo = pack_vec<E>(o1);
   hi = pack_vec<E>(o2);
@@ -228,11 +209,9 @@ __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, 
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const float c = e ? f.y : f.x, s = e ? f.w : f.z;
-      const float2 a = make_float2(k[4 * g + 2 * e], k[4 * g + 2 * e + 1]);  // (x_even, x_odd)
-      const float2 b = make_float2(a.y, a.x);
-      const float2 r = add2_rn(mul2_rn(a, make_float2(c, c)), mul2_rn(b, make_float2(-s, s)));
-      o[4 * g + 2 * e] = r.x;
-      o[4 * g + 2 * e + 1] = r.y;
+      const float x1 = k[4 * g + 2 * e], x2 = k[4 * g + 2 * e + 1];  // (even, odd)
+      o[4 * g + 2 * e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      o[4 * g + 2 * e + 1] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
     }
   }
   v = pack_vec<E>(o);

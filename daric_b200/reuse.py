@@ -49,6 +49,14 @@ class LoadPlan:
     total_bytes: int = 0
     extra: dict = field(default_factory=dict)
 
+    @property
+    def c_names(self):
+        """Layer-name array in C form, built once per plan."""
+        if "c_names" not in self.extra:
+            from ._lib import names_array
+            self.extra["c_names"] = names_array(self.layer_names)
+        return self.extra["c_names"]
+
 
 def build_load_plan(topo: CacheTopo, bpb: dict[str, int], block_ids_list: Sequence[Sequence[Sequence[int]]],
                     device, layer_name: Optional[str] = None, base_offset: int = 0) -> LoadPlan:
@@ -117,5 +125,5 @@ class ReusedKVLoader:
         if scores is not None:
             kw = dict(scores=scores, job_score_row=plan.job_layer, meta_score_col=score_col)
         self.copier.rerotate_scatter_pages(
-            plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat, plan.indices_offsets,
+            plan.c_names, plan.offsets, plan.byte_sizes, plan.indices_flat, plan.indices_offsets,
             plan.job_meta, mode, pos_a, pos_b, chunk_len, stream=stream, **kw)

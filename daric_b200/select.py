@@ -7,6 +7,7 @@ utils.py:406-465).
 from __future__ import annotations
 
 import ctypes as C
+import functools
 from collections.abc import Sequence
 from dataclasses import dataclass
 from typing import Optional
@@ -41,6 +42,45 @@ class Selection:
         return self.idx[layer, o:o + n], self.slot[layer, o:o + n]
 
 
+@functools.lru_cache(maxsize=256)
+def _select_args(L: int, T: int, seg_len, seg_col_off, seg_pos0, seg_blk_off, k, ratio, threshold):
+    """Host arrays of one selection shape (cached: serving repeats shapes)."""
+    lens = np.asarray(seg_len if seg_len is not None else (T,), np.int64)
+    nseg = len(lens)
+    cols = np.asarray(seg_col_off, np.int64) if seg_col_off is not None else \
+        np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    if len(cols) != nseg or (nseg and (cols.min() < 0 or (cols + lens).max() > T)):
+        raise RuntimeError("score segments must lie inside the score rows")
+    pos0 = np.asarray(seg_pos0 if seg_pos0 is not None else (0,) * nseg, np.int64)
+    blk = np.asarray(seg_blk_off if seg_blk_off is not None else (0,) * nseg, np.int64)
+    if threshold is not None:
+        mode, kk = _lib.SELECT_THRESHOLD, np.zeros(nseg, np.int64)
+        caps = lens.copy()
+    else:
+        mode = _lib.SELECT_TOPK
+        if k is None:
+            if ratio is None:
+                raise ValueError("score_select needs k, ratio or threshold")
+            kk = np.array([topk_count(int(n), ratio) for n in lens], np.int64)
+        else:
+            kk = np.broadcast_to(np.asarray(k, np.int64), (nseg,)).copy()
+        caps = np.minimum(kk, lens)
+    out_off = np.concatenate([[0], np.cumsum(caps)[:-1]]).astype(np.int64)
+    out_ld = max(int(caps.sum()), 1)
+    arrs = tuple(np.ascontiguousarray(a) for a in (lens, cols, pos0, blk, kk, out_off))
+    for a in arrs:
+        a.setflags(write=False)
+    return mode, nseg, out_ld, arrs
+
+
+def _tup(x):
+    if x is None:
+        return None
+    if isinstance(x, (int, np.integer)):
+        return int(x)
+    return tuple(int(v) for v in x)
+
+
 def score_select(scores: torch.Tensor, block_table: torch.Tensor, block_size: int, *,
                  seg_len: Optional[Sequence[int]] = None, seg_col_off: Optional[Sequence[int]] = None,
                  seg_pos0: Optional[Sequence[int]] = None, seg_blk_off: Optional[Sequence[int]] = None,
@@ -57,31 +97,9 @@ def score_select(scores: torch.Tensor, block_table: torch.Tensor, block_size: in
     if not block_table.is_cuda or block_table.dtype != torch.int32 or not block_table.is_contiguous():
         raise RuntimeError("block_table must be a contiguous CUDA int32 tensor")
     L, T = scores.shape
-    if seg_len is None:
-        seg_len = [T]
-    nseg = len(seg_len)
-    lens, lp = i64(seg_len)
-    cols, cp = i64(seg_col_off if seg_col_off is not None else np.concatenate([[0], np.cumsum(lens)[:-1]]))
-    if len(cols) != nseg or (nseg and (cols.min() < 0 or (cols + lens).max() > T)):
-        raise RuntimeError("score segments must lie inside the score rows")
-    pos0, pp = i64(seg_pos0 if seg_pos0 is not None else [0] * nseg)
-    blk, bp = i64(seg_blk_off if seg_blk_off is not None else [0] * nseg)
-    if threshold is not None:
-        mode, kk = _lib.SELECT_THRESHOLD, np.zeros(nseg, np.int64)
-        caps = lens.copy()
-    else:
-        mode = _lib.SELECT_TOPK
-        if k is None:
-            if ratio is None:
-                raise ValueError("score_select needs k, ratio or threshold")
-            kk = np.array([topk_count(int(n), ratio) for n in lens], np.int64)
-        else:
-            kk = np.broadcast_to(np.asarray(k, np.int64), (nseg,)).copy()
-        caps = np.minimum(kk, lens)
-    kk, kp = i64(kk)
-    out_off = np.concatenate([[0], np.cumsum(caps)[:-1]]).astype(np.int64)
-    oo, op = i64(out_off)
-    out_ld = max(int(caps.sum()), 1)
+    mode, nseg, out_ld, (lens, cols, pos0, blk, kk, out_off) = _select_args(
+        L, T, _tup(seg_len), _tup(seg_col_off), _tup(seg_pos0), _tup(seg_blk_off), _tup(k),
+        None if ratio is None else float(ratio), None if threshold is None else float(threshold))
     dev = scores.device.index
     if out is None:
         out = Selection(
@@ -93,12 +111,13 @@ def score_select(scores: torch.Tensor, block_table: torch.Tensor, block_size: in
         if out.idx.shape[1] < out_ld or out.idx.shape[0] < L or out.count.shape != (L, nseg):
             raise RuntimeError("preallocated selection output is too small")
         out.out_off = out_off
+    p64 = lambda a: a.ctypes.data_as(C.POINTER(C.c_int64))
     s = stream or torch.cuda.current_stream(dev).cuda_stream
     check(_lib.load().daric_score_select(
-        C.c_void_p(scores.data_ptr()), L, scores.stride(0), nseg, cp, lp, pp, kp, mode,
-        C.c_float(threshold if threshold is not None else 0.0), C.c_void_p(block_table.data_ptr()),
-        block_table.numel(), bp, int(block_size), C.c_void_p(out.idx.data_ptr()),
-        C.c_void_p(out.slot.data_ptr()), C.c_void_p(out.count.data_ptr()), out.idx.stride(0), op, dev,
+        C.c_void_p(scores.data_ptr()), L, scores.stride(0), nseg, p64(cols), p64(lens), p64(pos0), p64(kk),
+        mode, C.c_float(threshold if threshold is not None else 0.0), C.c_void_p(block_table.data_ptr()),
+        block_table.numel(), p64(blk), int(block_size), C.c_void_p(out.idx.data_ptr()),
+        C.c_void_p(out.slot.data_ptr()), C.c_void_p(out.count.data_ptr()), out.idx.stride(0), p64(out_off), dev,
         C.c_void_p(s)))
     return out
 
