@@ -2,9 +2,11 @@
 //
 //  * select_kernel : per (segment, layer) CTA, radix select of the k highest
 //    fp32 scores (8-bit digits, four histogram passes over an order-preserving
-//    32-bit key), then a stable compaction in token order that emits the
-//    recompute positions and their paged-KV slots. Threshold mode skips the
-//    radix passes. Ties at the k-th score go to the lower token index.
+//    32-bit key held in shared memory; per-warp histograms merged per pass),
+//    then a stable compaction in token order (warp ballots + one block scan)
+//    that emits the recompute positions and their paged-KV slots. Threshold
+//    mode skips the radix passes. Ties at the k-th score go to the lower
+//    token index.
 //  * ranges_kernel : expands [start, end) ranges of the DARIC policy
 //    (daric/adaption/policy.py:45-103) into positions and slots, the slot
 //    formula of the recompute sub-requests (integration/vllm/worker.py:310-346):
@@ -63,6 +65,7 @@ __device__ __forceinline__ uint32_t key_at(const float* row, const uint32_t* ske
 }
 
 __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
+  __shared__ uint32_t whist[kSelWarps][256];  // per-warp digit histograms
   __shared__ uint32_t hist[256];
   __shared__ int scan_sm[32];
   __shared__ uint32_t s_digit, s_above;
@@ -76,6 +79,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
   int64_t* oslot = p.out_slot + l * p.out_ld + sg.out_off;
   const bool topk = p.mode == DARIC_SELECT_TOPK;
   const bool staged = n <= kSmemKeys;
+  const int warp_id = threadIdx.x >> 5;
 
   uint32_t thr = 0;     // k-th largest key (top-k)
   int64_t take_eq = 0;  // keys equal to thr that are taken, lowest index first
@@ -108,16 +112,19 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
       int64_t rem = k;
       const int lane = threadIdx.x & 31;
       for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+        for (int b = threadIdx.x; b < kSelWarps * 256; b += blockDim.x) (&whist[0][0])[b] = 0;
         __syncthreads();
-        for (int64_t i = threadIdx.x; i - threadIdx.x < n; i += blockDim.x) {
-          const bool in = i < n;
-          const uint32_t key = in ? key_at(row, skeys, staged, i) : 0u;
-          const bool act = in && (key & mask) == prefix;
-          const uint32_t digit = act ? ((key >> shift) & 255u) : 256u + lane;
-          // lanes with the same digit add once (warp-aggregated atomics)
-          const uint32_t peers = __match_any_sync(0xffffffffu, digit);
-          if (act && lane == __ffs(peers) - 1) atomicAdd(&hist[digit], (uint32_t)__popc(peers));
+        uint32_t* wh = whist[warp_id];
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+          const uint32_t key = key_at(row, skeys, staged, i);
+          if ((key & mask) == prefix) atomicAdd(&wh[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+          uint32_t t = 0;
+#pragma unroll
+          for (int w = 0; w < kSelWarps; ++w) t += whist[w][b];
+          hist[b] = t;
         }
         __syncthreads();
         if (threadIdx.x < 32) {
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
   // [c0 + 512w, c0 + 512(w+1)) of each pass, as 16 rounds of 32 (lane = key),
   // so ballots give in-warp ranks and one block scan orders the warps.
   const bool use_keys = topk && !take_all;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, warp = warp_id;
   const uint32_t lt_mask = (1u << lane) - 1u;
   constexpr int R = 16;
   const int64_t span = (int64_t)kSelWarps * 32 * R;
