@@ -5,7 +5,8 @@
 // planes of a page) are moved by the copy engine with untiled
 // cp.async.bulk loads into a shared-memory stage (mbarrier completion,
 // NSTAGE stages in flight), the K rows are re-rotated in shared memory by
-// all threads, and the whole page goes back out with cp.async.bulk stores.
+// the consumer warps, and the whole page goes back out with cp.async.bulk
+// stores issued by a producer warp.
 // V bytes never pass through registers. Same byte mapping, block-0 skip,
 // rotation math and deviation scores as the SIMT kernels in page_kernels.cu.
 //
@@ -22,15 +23,18 @@ namespace daric {
 namespace {
 using namespace dev;
 
-constexpr int kBulkThreads = 512;
+constexpr int kConsumerWarps = 16;
+constexpr int kBulkThreads = kConsumerWarps * 32 + 32;  // + one producer warp
+constexpr int kMaxStages = 8;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-struct StageMeta {
+struct StageMeta {  // 24 bytes; kMaxStages of them fit [128, kBulkHeader)
   int64_t job;
   int64_t page_local;
   int32_t blk;
   int32_t skip;
 };
+static_assert(128 + kMaxStages * sizeof(StageMeta) <= kBulkHeader, "stage meta exceeds the header");
 
 // ------------------------------------------------------------- PTX ------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -115,18 +119,19 @@ __device__ __forceinline__ int64_t find_job(const JobDev* jobs, int64_t n, int64
 // the page's factor block (also in shared memory).
 template <class E, bool NEOX, bool SCORE>
 __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kreg, const float4* fac,
-                                                 int64_t tok0, int64_t len, float* tok_dev) {
+                                                 int64_t tok0, int64_t len, float* tok_dev, int tid,
+                                                 int nthreads) {
   constexpr int U = 4;
   const int ntask = L.nrows * L.pair_vecs;
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
   const int per_tok = L.half_rot / 2;
   const uint32_t base = smem_addr(kreg);
-  for (int b0 = threadIdx.x; b0 < ntask; b0 += U * blockDim.x) {
+  for (int b0 = tid; b0 < ntask; b0 += U * nthreads) {
     uint4 lo[U], hi[U];
     int off[U], slot[U], c[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int t = b0 + u * blockDim.x;
+      const int t = b0 + u * nthreads;
       off[u] = -1;
       if (t < ntask) {
         const int row = (int)fdiv((uint32_t)t, L.pair_div);
@@ -153,25 +158,35 @@ __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kre
   }
 }
 
-// Shared memory: [0,64) barriers | [64,256) stage meta | dev region |
-// stages (page data, then the page's factor block at fac_off).
+// Warp-specialised pipeline. Warps 0..kConsumerWarps-1 rotate; the last
+// warp's lane 0 is the producer: it issues the bulk loads of unit u into
+// stage u % NS (full[s] completes when the bytes land), waits until every
+// consumer warp has released the unit (empty[s]), issues the bulk stores,
+// and reuses the stage of the previous unit once its stores have read it.
+// Shared memory: [0,128) full/empty barriers | [128,512) stage meta |
+// per-stage deviation slots | stages (page data, then the page's factor
+// block at fac_off).
 template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE>
 __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch p, BulkGeom g) {
   using E = Elem<KVT>;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  StageMeta* meta = reinterpret_cast<StageMeta*>(smem + 64);
-  float* tok_dev = reinterpret_cast<float*>(smem + 256);
-  uint8_t* stages = smem + 256 + g.dev_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  StageMeta* meta = reinterpret_cast<StageMeta*>(smem + 128);
+  float* devs = reinterpret_cast<float*>(smem + kBulkHeader);  // NS x dev_stride floats
+  uint8_t* stages = smem + kBulkHeader + g.dev_bytes;
   const int NS = g.nstage;
+  const int dev_stride = g.dev_bytes / (4 * NS);
   const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool producer = warp == kConsumerWarps;
+  constexpr int kConsumers = kConsumerWarps * 32;
 
   int64_t ubeg, uend;
   cta_range(p.total_units, ubeg, uend);
   if (ubeg >= uend) return;
   const int64_t n = uend - ubeg;
 
-  int64_t pj = 0;  // producer's job cursor (thread 0)
   auto region_src = [&](const JobDev& j, const LayerDev& L, int64_t pl, int32_t blk, int pf) -> const uint8_t* {
     if (GATHER) return L.base + (int64_t)pf * L.prefix_stride + (int64_t)blk * L.page_stride;
     return p.store + j.stg_off + ((int64_t)pf * j.n_sel + pl) * L.suffix;
@@ -183,91 +198,125 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   auto unit_rotates = [&](const JobDev& j, const LayerDev& L) -> bool {
     return ROTATE && j.meta >= 0 && L.has_rot && p.metas[j.meta].rotate;
   };
-  auto issue = [&](int64_t u, int s) {
-    while (pj + 1 < p.num_jobs && p.jobs[pj + 1].unit_begin <= u) ++pj;
-    const JobDev j = p.jobs[pj];
-    const LayerDev& L = p.layers[j.layer];
-    const int64_t pl = u - j.unit_begin;
-    const int32_t blk = __ldg(&p.indices[j.idx_off + pl]);
-    int skip = blk == 0;
-    if (!skip && (blk < 0 || blk >= L.num_pages)) {
-      atomicOr(p.err, DEV_ERR_BLOCK_RANGE);
-      skip = 1;
-    }
-    meta[s] = StageMeta{pj, pl, blk, skip};
-    if (skip) {
-      mbar_arrive(&bars[s]);
-      return;
-    }
-    uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-    const bool rot = unit_rotates(j, L);
-    const uint32_t fbytes = rot ? (uint32_t)page_factor_bytes(L.page_size, L.half_rot) : 0u;
-    mbar_arrive_expect_tx(&bars[s], (uint32_t)(L.prefix_size * L.suffix) + fbytes);
-    for (int pf = 0; pf < L.prefix_size; ++pf)
-      bulk_load(buf + (size_t)pf * L.suffix, region_src(j, L, pl, blk, pf), (uint32_t)L.suffix, &bars[s]);
-    if (rot)
-      bulk_load(buf + g.fac_off, p.fac + (j.fac_tok + pl * L.page_size) * (L.half_rot / 2), fbytes, &bars[s]);
-  };
 
   if (tid == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
     mbar_init_fence();
-    pj = find_job(p.jobs, p.num_jobs, ubeg);
-    for (int s = 0; s < NS - 1 && s < n; ++s) issue(ubeg + s, s);
   }
+  if (SCORE)
+    for (int q = tid; q < NS * dev_stride; q += blockDim.x) devs[q] = 0.f;
   __syncthreads();
 
-  int64_t i = 0;
-  bool failed = false;
-  for (; i < n; ++i) {
+  if (producer) {
+    if (lane != 0) return;
+    int64_t pj = find_job(p.jobs, p.num_jobs, ubeg);
+    auto issue = [&](int64_t i) {  // loads of unit ubeg+i into stage i % NS
+      const int s = (int)(i % NS);
+      const int64_t u = ubeg + i;
+      while (pj + 1 < p.num_jobs && p.jobs[pj + 1].unit_begin <= u) ++pj;
+      const JobDev j = p.jobs[pj];
+      const LayerDev& L = p.layers[j.layer];
+      const int64_t pl = u - j.unit_begin;
+      const int32_t blk = __ldg(&p.indices[j.idx_off + pl]);
+      int skip = blk == 0;
+      if (!skip && (blk < 0 || blk >= L.num_pages)) {
+        atomicOr(p.err, DEV_ERR_BLOCK_RANGE);
+        skip = 1;
+      }
+      meta[s] = StageMeta{pj, pl, blk, skip};
+      if (skip) {
+        mbar_arrive(&full[s]);
+        return;
+      }
+      uint8_t* buf = stages + (size_t)s * g.stage_bytes;
+      const bool rot = unit_rotates(j, L);
+      const uint32_t fbytes = rot ? (uint32_t)page_factor_bytes(L.page_size, L.half_rot) : 0u;
+      mbar_arrive_expect_tx(&full[s], (uint32_t)(L.prefix_size * L.suffix) + fbytes);
+      for (int pf = 0; pf < L.prefix_size; ++pf)
+        bulk_load(buf + (size_t)pf * L.suffix, region_src(j, L, pl, blk, pf), (uint32_t)L.suffix, &full[s]);
+      if (rot)
+        bulk_load(buf + g.fac_off, p.fac + (j.fac_tok + pl * L.page_size) * (L.half_rot / 2), fbytes, &full[s]);
+    };
+    int64_t issued = 0;
+    for (; issued < NS - 1 && issued < n; ++issued) issue(issued);
+    bool prev_stored = false;  // unit i-1 has a pending store group
+    int64_t i = 0;
+    for (; i < n; ++i) {
+      const int s = (int)(i % NS);
+      if (!mbar_wait(&empty[s], (uint32_t)((i / NS) & 1))) {
+        atomicOr(p.err, DEV_ERR_TIMEOUT);
+        break;
+      }
+      const StageMeta st = meta[s];
+      bool stored = false;
+      if (!st.skip) {
+        const JobDev j = p.jobs[st.job];
+        const LayerDev& L = p.layers[j.layer];
+        uint8_t* buf = stages + (size_t)s * g.stage_bytes;
+        for (int pf = 0; pf < L.prefix_size; ++pf)
+          bulk_store(region_dst(j, L, st.page_local, st.blk, pf), buf + (size_t)pf * L.suffix,
+                     (uint32_t)L.suffix);
+        bulk_commit();
+        stored = true;
+      }
+      if (SCORE) {
+        const JobDev j = p.jobs[st.job];
+        if (j.score_row >= 0 && j.meta >= 0) {
+          const LayerDev& L = p.layers[j.layer];
+          const MetaDev m = p.metas[j.meta];
+          const int64_t tok0 = st.page_local * L.page_size;
+          float* out = p.scores + (int64_t)j.score_row * p.score_ld + m.score_col + tok0;
+          float* dv = devs + s * dev_stride;
+          for (int q = 0; q < L.page_size; ++q) {
+            if (tok0 + q < m.len) out[q] = dv[q];
+            dv[q] = 0.f;
+          }
+        }
+      }
+      // the next load goes into the stage of unit i-1: its stores must have
+      // read it (unit i's group, committed last, may still be pending)
+      if (issued < n) {
+        if (prev_stored) {
+          if (stored) bulk_wait_read<1>(); else bulk_wait_read<0>();
+        }
+        issue(issued);
+        ++issued;
+      }
+      prev_stored = stored;
+    }
+    if (i < n) {
+      // timed out: drain the loads still in flight into this CTA's stages
+      for (int64_t k = i + 1; k < issued; ++k) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
+    }
+    bulk_wait_all();
+    return;
+  }
+
+  // consumers
+  for (int64_t i = 0; i < n; ++i) {
     const int s = (int)(i % NS);
+    if (!mbar_wait(&full[s], (uint32_t)((i / NS) & 1))) {
+      atomicOr(p.err, DEV_ERR_TIMEOUT);
+      break;
+    }
     const StageMeta st = meta[s];
     const JobDev j = p.jobs[st.job];
     const LayerDev& L = p.layers[j.layer];
-    uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-    const bool rotate = !st.skip && unit_rotates(j, L);
-    const bool scoring = SCORE && j.score_row >= 0 && j.meta >= 0;
-    const int64_t len = (ROTATE && j.meta >= 0) ? p.metas[j.meta].len : 0;
-    const int64_t tok0 = st.page_local * L.page_size;
-    if (scoring)
-      for (int q = tid; q < L.page_size; q += blockDim.x) tok_dev[q] = 0.f;
-    const bool ok = mbar_wait(&bars[s], (uint32_t)((i / NS) & 1));
-    if (__syncthreads_or(!ok)) {
-      failed = true;
-      break;
-    }
-    if (rotate)
+    if (!st.skip && unit_rotates(j, L)) {
+      uint8_t* buf = stages + (size_t)s * g.stage_bytes;
+      const int64_t len = p.metas[j.meta].len;
+      const int64_t tok0 = st.page_local * L.page_size;
       rotate_rows_smem<E, NEOX, SCORE>(L, buf + (size_t)L.k_prefix * L.suffix,
-                                       reinterpret_cast<const float4*>(buf + g.fac_off), tok0, len, tok_dev);
-    fence_proxy_async();
-    __syncthreads();
-    if (tid == 0 && !st.skip) {
-      for (int pf = 0; pf < L.prefix_size; ++pf)
-        bulk_store(region_dst(j, L, st.page_local, st.blk, pf), buf + (size_t)pf * L.suffix, (uint32_t)L.suffix);
-      bulk_commit();
+                                       reinterpret_cast<const float4*>(buf + g.fac_off), tok0, len,
+                                       devs + s * dev_stride, tid, kConsumers);
+      fence_proxy_async();
     }
-    if (scoring) {
-      float* out = p.scores + (int64_t)j.score_row * p.score_ld + p.metas[j.meta].score_col + tok0;
-      for (int q = tid; q < L.page_size; q += blockDim.x)
-        if (tok0 + q < len) out[q] = rotate ? tok_dev[q] : 0.f;
-    }
-    // Unit i+NS-1 reuses the stage of unit i-1, whose stores must have
-    // finished reading it (the newest bulk group, unit i's, may still run).
-    const int64_t nxt = i + NS - 1;
-    if (tid == 0 && nxt < n) {
-      if (st.skip) bulk_wait_read<0>(); else bulk_wait_read<1>();
-      issue(ubeg + nxt, (int)(nxt % NS));
-    }
-    __syncthreads();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (failed && tid == 0) {
-    atomicOr(p.err, DEV_ERR_TIMEOUT);
-    // drain the loads still in flight into this CTA's shared memory
-    const int64_t issued = (i + NS - 1 < n) ? i + NS - 1 : n;
-    for (int64_t k = i; k < issued; ++k) mbar_wait(&bars[k % NS], (uint32_t)((k / NS) & 1));
-  }
-  if (tid == 0) bulk_wait_all();
-  __syncthreads();
 }
 
 // ------------------------------------------------------------ launch ----

@@ -407,10 +407,14 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
   }
   const size_t fac_off = round_up(data, 128);
   const size_t stage = round_up(fac_off + fac, 128);
-  dev = round_up(dev, 128);
-  if (data == 0 || data + fac >= (1u << 20) || (size_t)dc.smem_optin < 256 + dev) return g;
-  const size_t ns = std::min<size_t>(4, ((size_t)dc.smem_optin - 256 - dev) / stage);
+  if (data == 0 || data + fac >= (1u << 20)) return g;
+  // stages fill what is left after the header and one deviation slot array
+  // per stage
+  size_t ns = 0;
+  for (size_t k = 8; k >= 2; --k)
+    if (kBulkHeader + k * round_up(dev, 16) + 128 + k * stage <= (size_t)dc.smem_optin) { ns = k; break; }
   if (ns < 2) return g;
+  dev = round_up(ns * round_up(dev, 16), 128);
   g.nstage = (int32_t)ns;
   g.stage_bytes = (int32_t)stage;
   g.fac_off = (int32_t)fac_off;

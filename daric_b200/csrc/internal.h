@@ -237,8 +237,11 @@ struct BulkGeom {
   int32_t dev_bytes;
 };
 
+// Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
+constexpr int kBulkHeader = 512;
+
 inline size_t bulk_smem_bytes(const BulkGeom& g) {
-  return 256 + (size_t)g.dev_bytes + (size_t)g.nstage * g.stage_bytes;
+  return kBulkHeader + (size_t)g.dev_bytes + (size_t)g.nstage * g.stage_bytes;
 }
 
 // ------------------------------------------------------------ launchers --
