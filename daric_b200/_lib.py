@@ -63,6 +63,9 @@ SIGNATURES: dict[str, tuple] = {
     "daric_score_select": (
         C.c_int, [_vp, C.c_int64, C.c_int64, C.c_int64, _i64p, _i64p, _i64p, _i64p, C.c_int, C.c_float,
                   _vp, C.c_int64, _i64p, C.c_int64, _vp, _vp, _vp, C.c_int64, _i64p, C.c_int, _vp]),
+    "daric_score_select_noalloc": (
+        C.c_int, [_vp, C.c_int64, C.c_int64, C.c_int64, _i64p, _i64p, _i64p, _i64p, C.c_int, C.c_float,
+                  _vp, C.c_int64, _i64p, C.c_int64, _vp, _vp, _vp, C.c_int64, _i64p, C.c_int, _vp]),
     "daric_ptrs_to_slots": (
         C.c_int, [C.c_int64, _i64p, _i64p, _i64p, _vp, C.c_int64, C.c_int64, _vp, _vp, C.c_int, _vp]),
 }

@@ -666,6 +666,15 @@ void resolve_rotary(LayerHost& L, int kv_dtype, const void* table, int tab_dtype
 
 }  // namespace
 
+// Error reporting for entry points implemented in other translation units.
+namespace daric {
+void record_error(int code, const char* msg) {
+  (void)code;
+  g_last_error = msg;
+}
+void clear_error() { g_last_error.clear(); }
+}  // namespace daric
+
 // ===================================================================== C ==
 extern "C" {
 

@@ -261,4 +261,9 @@ void launch_ranges_to_slots(const RangeLaunch& p, cudaStream_t s);
 
 int* device_error_word(int device);  // per-device error word (lazily created)
 
+// Last-error hooks of the C boundary (capi.cpp) for entry points defined in
+// other translation units.
+void record_error(int code, const char* msg);
+void clear_error();
+
 }  // namespace daric

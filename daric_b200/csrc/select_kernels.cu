@@ -290,3 +290,142 @@ void launch_ranges_to_slots(const RangeLaunch& p, cudaStream_t s) {
 }
 
 }  // namespace daric
+
+// ---------------------------------------------------------------------------
+// daric_score_select_noalloc: the selection above for callers that must not
+// allocate device memory once running (a serving process whose free device
+// memory all went to its KV cache at start-up, or a host whose memory pool
+// owns every device allocation). The per-request descriptors, which
+// daric_score_select keeps in library-allocated scratch, live in the fixed
+// file-scope array below; the call allocates nothing (no cudaMalloc /
+// cudaFree, no host containers on the success path).
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int kNoallocMaxSegs = DARIC_NOALLOC_MAX_SEGMENTS;
+constexpr size_t kNoallocSegBytes = (size_t)kNoallocMaxSegs * sizeof(daric::SelSegDev);  // 48 KiB
+constexpr int kNoallocMaxDevices = 64;
+}  // namespace
+
+// [kNoallocMaxSegs descriptors][256 bytes: device error word]. In host code
+// this name only stands in for the array; its device address comes from
+// cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_select_scratch[kNoallocSegBytes + 256];
+
+namespace {
+
+std::mutex g_noalloc_mu;                              // guards the host staging and set-up
+daric::SelSegDev g_noalloc_host[kNoallocMaxSegs];     // host staging of one call's descriptors
+unsigned char* g_noalloc_dev[kNoallocMaxDevices];     // device address of the array, per device
+
+// Set-up, once per device, with that device current: the array's device
+// address and the kernel's dynamic shared-memory limit.
+unsigned char* noalloc_scratch(int device) {
+  if (g_noalloc_dev[device]) return g_noalloc_dev[device];
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_select_scratch);
+  if (e != cudaSuccess || ptr == nullptr)
+    throw daric::Error(DARIC_ERR_CUDA, std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+  e = cudaFuncSetAttribute(daric::select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           daric::kSmemKeys * (int)sizeof(uint32_t));
+  if (e != cudaSuccess)
+    throw daric::Error(DARIC_ERR_CUDA, std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(e));
+  g_noalloc_dev[device] = static_cast<unsigned char*>(ptr);
+  return g_noalloc_dev[device];
+}
+
+void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, int64_t num_segs,
+                    const int64_t* seg_col_off, const int64_t* seg_len, const int64_t* seg_pos0,
+                    const int64_t* seg_k, int mode, float threshold, const int32_t* block_table,
+                    int64_t block_table_numel, const int64_t* seg_blk_off, int64_t block_size, int32_t* out_idx,
+                    int64_t* out_slot, int32_t* out_count, int64_t out_ld, const int64_t* out_off, int device,
+                    cudaStream_t stream) {
+  using daric::Error;
+  DARIC_CHECK(mode == DARIC_SELECT_TOPK || mode == DARIC_SELECT_THRESHOLD, "unknown selection mode");
+  if (num_layers <= 0 || num_segs <= 0) return;
+  DARIC_CHECK(num_segs <= kNoallocMaxSegs,
+              "daric_score_select_noalloc: " + std::to_string(num_segs) +
+                  " segments exceed its fixed scratch of DARIC_NOALLOC_MAX_SEGMENTS = " +
+                  std::to_string(kNoallocMaxSegs));
+  DARIC_CHECK(num_layers <= 65535, "score_select: at most 65535 layers per call");
+  DARIC_CHECK(device >= 0 && device < kNoallocMaxDevices, "device index out of range");
+  DARIC_CHECK(scores && out_idx && out_slot && out_count, "NULL device pointer");
+  DARIC_CHECK(seg_col_off && seg_len && seg_pos0 && seg_blk_off && out_off, "NULL segment array");
+  DARIC_CHECK(mode != DARIC_SELECT_TOPK || seg_k, "TOPK needs seg_k");
+  DARIC_CHECK(block_size > 0, "block_size must be positive");
+  DARIC_CHECK(block_table != nullptr || block_table_numel == 0, "block_table is NULL");
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) throw Error(DARIC_ERR_CUDA, "cudaGetDevice failed");
+  if (prev != device && cudaSetDevice(device) != cudaSuccess) throw Error(DARIC_ERR_CUDA, "cudaSetDevice failed");
+  struct Restore {
+    int d, p;
+    ~Restore() { if (d != p && p >= 0) cudaSetDevice(p); }
+  } restore{device, prev};
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  unsigned char* scratch = noalloc_scratch(device);
+  for (int64_t s = 0; s < num_segs; ++s) {
+    daric::SelSegDev& d = g_noalloc_host[s];
+    d.col_off = seg_col_off[s];
+    d.len = seg_len[s];
+    d.pos0 = seg_pos0[s];
+    d.k = mode == DARIC_SELECT_TOPK ? seg_k[s] : 0;
+    d.blk_off = seg_blk_off[s];
+    d.out_off = out_off[s];
+    DARIC_CHECK(d.col_off >= 0 && d.len >= 0 && d.pos0 >= 0 && d.k >= 0 && d.blk_off >= 0 && d.out_off >= 0,
+                "negative segment field at segment " + std::to_string(s));
+    DARIC_CHECK(d.col_off + d.len <= score_ld, "segment " + std::to_string(s) + " exceeds the score row (score_ld)");
+    DARIC_CHECK(d.pos0 + d.len <= INT32_MAX, "positions exceed int32");
+    const int64_t cap = mode == DARIC_SELECT_TOPK ? (d.k < d.len ? d.k : d.len) : d.len;
+    DARIC_CHECK(d.out_off + cap <= out_ld, "segment " + std::to_string(s) + " output exceeds out_ld");
+  }
+  // Pageable source: the copy is staged by the driver before it returns, so
+  // the host staging can be reused by the next call right away. The error
+  // word starts at zero on every call.
+  cudaError_t e = cudaMemcpyAsync(scratch, g_noalloc_host, (size_t)num_segs * sizeof(daric::SelSegDev),
+                                  cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(scratch + kNoallocSegBytes, 0, sizeof(int), stream);
+  if (e != cudaSuccess) throw Error(DARIC_ERR_CUDA, std::string("noalloc select copy: ") + cudaGetErrorString(e));
+  daric::SelectLaunch p{};
+  p.scores = scores;
+  p.num_layers = num_layers;
+  p.score_ld = score_ld;
+  p.num_segs = num_segs;
+  p.segs = reinterpret_cast<const daric::SelSegDev*>(scratch);
+  p.mode = mode;
+  p.threshold = threshold;
+  p.block_table = block_table;
+  p.block_table_numel = block_table_numel;
+  p.block_size = block_size;
+  p.out_idx = out_idx;
+  p.out_slot = out_slot;
+  p.out_count = out_count;
+  p.out_ld = out_ld;
+  p.err = reinterpret_cast<int*>(scratch + kNoallocSegBytes);
+  const dim3 grid((unsigned)num_segs, (unsigned)num_layers, 1);
+  daric::select_kernel<<<grid, daric::kSelThreads, daric::kSmemKeys * sizeof(uint32_t), stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) throw Error(DARIC_ERR_CUDA, std::string("noalloc select launch: ") + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" int daric_score_select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld,
+                                          int64_t num_segs, const int64_t* seg_col_off, const int64_t* seg_len,
+                                          const int64_t* seg_pos0, const int64_t* seg_k, int mode, float threshold,
+                                          const int32_t* block_table, int64_t block_table_numel,
+                                          const int64_t* seg_blk_off, int64_t block_size, int32_t* out_idx,
+                                          int64_t* out_slot, int32_t* out_count, int64_t out_ld,
+                                          const int64_t* out_off, int device, void* stream) {
+  try {
+    select_noalloc(scores, num_layers, score_ld, num_segs, seg_col_off, seg_len, seg_pos0, seg_k, mode, threshold,
+                   block_table, block_table_numel, seg_blk_off, block_size, out_idx, out_slot, out_count, out_ld,
+                   out_off, device, (cudaStream_t)stream);
+    daric::clear_error();
+    return DARIC_OK;
+  } catch (const daric::Error& err) {
+    daric::record_error(err.code, err.what());
+    return err.code;
+  } catch (const std::exception& err) {
+    daric::record_error(DARIC_ERR_STATE, err.what());
+    return DARIC_ERR_STATE;
+  }
+}

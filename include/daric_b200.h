@@ -222,6 +222,34 @@ DARIC_API int daric_score_select(const float* scores, int64_t num_layers, int64_
                        int32_t* out_idx, int64_t* out_slot, int32_t* out_count, int64_t out_ld,
                        const int64_t* out_off, int device, void* stream);
 
+/* Largest number of requests (segments) one daric_score_select_noalloc call
+ * accepts: the size of its fixed scratch. */
+#define DARIC_NOALLOC_MAX_SEGMENTS 1024
+
+/* Recompute selection that allocates no device memory. No counterpart in the
+ * reference. Same arguments, checks and results as daric_score_select, for
+ * callers that must not call cudaMalloc once they are running: a serving
+ * process that gave all free device memory to its KV cache at start-up (any
+ * later device allocation fails or breaks that budget), or a host whose
+ * memory pool owns every device allocation. The per-request descriptors go
+ * to a fixed device array inside the library (48 KiB + 256 B, held by every
+ * GPU that loads the library until exit) instead of library-allocated
+ * scratch, so at most DARIC_NOALLOC_MAX_SEGMENTS requests per call; more are
+ * rejected with DARIC_ERR_INVALID. The caller still passes the inputs and
+ * outputs. The first call on each device looks up that array's device
+ * address and sets the kernel's shared-memory limit; make that first call
+ * before any stream capture. All calls share the one array: calls that
+ * overlap on the GPU (other streams or threads) race on it and must be
+ * serialised by the caller. A block-table index outside the table yields
+ * slot -1 (the device error bits of daric_device_errors are not used). */
+DARIC_API int daric_score_select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld,
+                                         int64_t num_segs, const int64_t* seg_col_off, const int64_t* seg_len,
+                                         const int64_t* seg_pos0, const int64_t* seg_k, int mode, float threshold,
+                                         const int32_t* block_table, int64_t block_table_numel,
+                                         const int64_t* seg_blk_off, int64_t block_size, int32_t* out_idx,
+                                         int64_t* out_slot, int32_t* out_count, int64_t out_ld,
+                                         const int64_t* out_off, int device, void* stream);
+
 /* DARIC-policy ranges -> recompute index list + slot mapping. Expands the
  * [start, end) ranges of DARICPolicy.get_recompute_ptrs (policy.py:45-103) the
  * way the recompute sub-requests do (worker.py:324-344, utils.py:406-465):
