@@ -37,7 +37,7 @@ import torch
 ROOT = Path(__file__).resolve().parent
 METRIC = "reused-KV GB/s per GPU (fraction of HBM peak); µs per 8K-token prompt, 1/2/4/8 GPU"
 CFG = dict(layers=32, kv_heads=8, head_dim=128, block_size=16, tokens=8192, chunk=512, theta=5e5,
-           ratio=0.15, max_pos=8192)
+           ratio=0.15, max_pos=8192)  # config 2, also the reference arm's sample
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -61,65 +61,127 @@ def rope_table(max_pos, rot_dim, base, dtype):
     return torch.cat((f.cos(), f.sin()), dim=-1).to(dtype)
 
 
-class Workload:
-    """Synthetic config-2 inputs, seeded per rank."""
+CONFIGS = {
+    # one 8K prompt of 16 reused 512-token chunks (default)
+    2: dict(name="llama3-8b-8k-prompt", layers=32, kv_heads=8, head_dim=128, block_size=16, theta=5e5,
+            ratio=0.15, requests=1, chunks=16, chunk_len=(512, 512), suffix=0, scores="lognormal", tp=False),
+    # 64 requests x 6 chunks of U[256, 1024] (multiple of 16) + 64 uncached tokens
+    3: dict(name="qwen2.5-7b-64req", layers=28, kv_heads=4, head_dim=128, block_size=16, theta=1e6,
+            ratio=0.10, requests=64, chunks=6, chunk_len=(256, 1024), suffix=64, scores="lognormal", tp=False),
+    # 70B shape, 32K prompt of 64 x 512 chunks, KV heads split over the ranks,
+    # deviation scores all-reduced before a top-20% selection
+    4: dict(name="llama3-70b-32k-tp", layers=80, kv_heads=8, head_dim=128, block_size=16, theta=5e5,
+            ratio=0.20, requests=1, chunks=64, chunk_len=(512, 512), suffix=0, scores="deviation", tp=True),
+}
 
-    def __init__(self, device, seed=0):
+
+class Workload:
+    """Synthetic inputs of one config, seeded: block layout and positions are
+    shared by all ranks (seed), values differ per rank (seed + rank)."""
+
+    def __init__(self, device, seed=0, config=2, rank=0, world=1):
         from daric_b200.reuse import ReusedKVLoader, layer_block_bytes
+        from daric_b200.shard import tp_head_range
         from daric_b200.topo import CacheTopo
-        c = CFG
+        c = CONFIGS[config]
+        self.cfg = c
         self.device = device
         g = torch.Generator(device="cpu").manual_seed(seed)
-        L, H, D, bs, T, C = c["layers"], c["kv_heads"], c["head_dim"], c["block_size"], c["tokens"], c["chunk"]
-        M = T // C
-        pages_per_chunk = C // bs
-        nb = T // bs + 64                      # + null block 0 and free blocks
+        L, D, bs = c["layers"], c["head_dim"], c["block_size"]
+        H = c["kv_heads"]
+        if c["tp"]:
+            h0, h1 = tp_head_range(rank, world, H)
+            H = h1 - h0
+        self.heads = H
+        # chunk lengths per request, placement and shuffled saved positions
+        lo, hi = c["chunk_len"]
+        reqs = []
+        for r in range(c["requests"]):
+            lens = [lo] * c["chunks"] if lo == hi else \
+                [int(x) * bs for x in torch.randint(lo // bs, hi // bs + 1, (c["chunks"],), generator=g)]
+            reqs.append(lens)
+        self.chunk_len, self.new_pos, self.old_pos, self.req_of = [], [], [], []
+        self.req_tokens = []
+        for r, lens in enumerate(reqs):
+            starts = np.concatenate([[0], np.cumsum(lens)[:-1]]).tolist()
+            order = torch.randperm(len(lens), generator=g).tolist()
+            shuffled = [lens[o] for o in order]
+            saved_starts = np.concatenate([[0], np.cumsum(shuffled)[:-1]]).tolist()
+            saved = [0] * len(lens)
+            for slot, o in enumerate(order):
+                saved[o] = saved_starts[slot]
+            self.chunk_len += lens
+            self.new_pos += starts
+            self.old_pos += saved
+            self.req_of += [r] * len(lens)
+            self.req_tokens.append(sum(lens))
+        M = len(self.chunk_len)
+        pages = [n // bs for n in self.chunk_len]
+        total_pages = sum(pages)
+        nb = total_pages + c["requests"] * (c["suffix"] // bs + 1) + 64
+        perm = (torch.randperm(nb - 1, generator=g)[:total_pages] + 1).tolist()
+        self.chunk_blocks, k = [], 0
+        for n in pages:
+            self.chunk_blocks.append(perm[k:k + n])
+            k += n
+        self.block_table = torch.tensor(perm, dtype=torch.int32, device=device)  # requests back to back
+        self.req_blk_off = np.concatenate([[0], np.cumsum([sum(pages[i] for i in range(M) if self.req_of[i] == r)
+                                                           for r in range(c["requests"])])[:-1]]).astype(np.int64)
+        max_pos = max(o + n for o, n in zip(self.old_pos + self.new_pos, self.chunk_len * 2)) + c["suffix"] + 1
+        self.table = rope_table(max_pos, D, c["theta"], torch.bfloat16).to(device)
         self.names = [f"model.layers.{i}.self_attn.attn" for i in range(L)]
         self.kv = {n: torch.zeros((2, nb, bs, H, D), dtype=torch.bfloat16, device=device) for n in self.names}
-        perm = torch.randperm(nb - 1, generator=g)[: T // bs] + 1
-        self.chunk_blocks = [perm[m * pages_per_chunk:(m + 1) * pages_per_chunk].tolist() for m in range(M)]
-        self.block_table = perm.to(torch.int32).to(device)
-        # chunk m is placed at m*C; it was saved at a shuffled slot
-        order = torch.randperm(M, generator=g).tolist()
-        self.new_pos = [m * C for m in range(M)]
-        self.old_pos = [order[m] * C for m in range(M)]
-        self.chunk_len = [C] * M
-        self.table = rope_table(c["max_pos"], D, c["theta"], torch.bfloat16).to(device)
         topo = CacheTopo.single_group(self.names, bs, layer_block_bytes(self.kv[self.names[0]], False), False)
-        total = M * L * 2 * pages_per_chunk * bs * H * D * 2
+        per_tok = L * 2 * H * D * 2
+        total = sum(self.chunk_len) * per_tok
         self.staging = torch.empty(total, dtype=torch.uint8, device=device)
-        gd = torch.Generator(device=device).manual_seed(seed + 1)
-        vals = self.staging.view(torch.bfloat16).view(M, L, 2, pages_per_chunk, bs, H, D)
+        gd = torch.Generator(device=device).manual_seed(seed + 1 + rank)
+        off = 0
         for m in range(M):  # K,V ~ N(0,1); 4 K channels per head x8
-            x = torch.randn((L, 2, pages_per_chunk, bs, H, D), generator=gd, device=device)
+            n = self.chunk_len[m] * per_tok
+            x = torch.randn((L, 2, pages[m], bs, H, D), generator=gd, device=device)
             ch = torch.randperm(D, generator=g)[:4].to(device)
             x[:, 0, ..., ch] *= 8.0
-            vals[m].copy_(x.to(torch.bfloat16))
+            self.staging[off:off + n].view(torch.bfloat16).copy_(x.reshape(-1).to(torch.bfloat16))
+            off += n
         del x
-        self.loader = ReusedKVLoader(self.kv, topo, self.staging,
-                                     {n: (self.table, D, True) for n in self.names})
+        self.loader = ReusedKVLoader(self.kv, topo, self.staging, {n: (self.table, D, True) for n in self.names})
         self.plan = self.loader.plan([(b,) for b in self.chunk_blocks])
         assert self.plan.total_bytes == total
-        sc = torch.distributions.LogNormal(0.0, 1.0).sample((L, T))
-        spikes = torch.rand(L, T, generator=g) < 0.02
-        self.scores_host = torch.where(spikes, sc * 20, sc).float().contiguous()
+        T = sum(self.chunk_len)
+        self.score_col = np.concatenate([[0], np.cumsum(self.chunk_len)[:-1]]).astype(np.int64)
+        if c["scores"] == "lognormal":
+            sc = torch.distributions.LogNormal(0.0, 1.0).sample((L, T))
+            spikes = torch.rand(L, T, generator=g) < 0.02
+            self.scores_host = torch.where(spikes, sc * 20, sc).float().contiguous()
+        else:
+            self.scores_host = torch.zeros((L, T), dtype=torch.float32)
         self.scores = self.scores_host.to(device)
         self.sel = None
         self.bytes = algorithmic_bytes(T, L, H, D)
         self.tokens = T
+        self.seg_len = list(self.req_tokens)
+        self.seg_blk_off = self.req_blk_off.tolist()
 
     def load(self, stream=0):
+        kw = {}
+        if self.cfg["scores"] == "deviation":
+            kw = dict(scores=self.scores, score_col=self.score_col)
         self.loader.load(self.plan, mode="flexible", pos_a=self.old_pos, pos_b=self.new_pos,
-                         chunk_len=self.chunk_len, stream=stream)
+                         chunk_len=self.chunk_len, stream=stream, **kw)
 
     def select(self, scores=None):
         from daric_b200.select import score_select
         self.sel = score_select(scores if scores is not None else self.scores, self.block_table,
-                                CFG["block_size"], ratio=CFG["ratio"], out=self.sel)
+                                self.cfg["block_size"], seg_len=self.seg_len, seg_blk_off=self.seg_blk_off,
+                                ratio=self.cfg["ratio"], out=self.sel)
         return self.sel
 
     def step(self):
         self.load()
+        if self.cfg["tp"]:
+            from daric_b200.shard import allreduce_scores
+            allreduce_scores(self.scores)
         return self.select()
 
 
@@ -261,7 +323,12 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     from daric_b200 import _lib
-    wl = Workload(dev, seed=rank)
+    cfg = CONFIGS[args.config]
+    tp = cfg["tp"]
+    # data parallel: every rank loads its own requests; tensor parallel: one
+    # prompt, each rank its KV-head shard
+    wl = Workload(dev, seed=0 if tp else rank, config=args.config, rank=rank if tp else 0,
+                  world=world if tp else 1)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -282,6 +349,9 @@ def run_ours(args):
             ev[i][0].record(stream)
             wl.load()
             ev[i][1].record(stream)
+            if tp:
+                from daric_b200.shard import allreduce_scores
+                allreduce_scores(wl.scores)
             wl.select()
         host_us = (time.perf_counter() - h0) / args.steps * 1e6  # enqueue time per step
         end.record(stream)
@@ -299,7 +369,7 @@ def run_ours(args):
     # ---- e2e: public API from pinned host buffers
     from daric_b200.cache_ops import batched_memcpy_h2d
     host_shm = torch.empty(wl.staging.numel(), dtype=torch.uint8).pin_memory()
-    host_shm.copy_(wl.staging.cpu())
+    host_shm.copy_(wl.staging)
     host_scores = wl.scores_host.pin_memory()
     sel = wl.select()
     out_idx = torch.empty(sel.idx.shape, dtype=sel.idx.dtype).pin_memory()
@@ -311,8 +381,12 @@ def run_ours(args):
 
     def e2e_step():
         batched_memcpy_h2d(host_shm, wl.staging, chunk_off, chunk_off, chunk_size)
-        wl.scores.copy_(host_scores, non_blocking=True)
+        if not tp:
+            wl.scores.copy_(host_scores, non_blocking=True)
         wl.load()
+        if tp:
+            from daric_b200.shard import allreduce_scores
+            allreduce_scores(wl.scores)
         s = wl.select()
         out_idx.copy_(s.idx, non_blocking=True)
         out_slot.copy_(s.slot, non_blocking=True)
@@ -329,11 +403,15 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    t = torch.tensor([e2e_ms], device=dev)
+    t = torch.tensor([e2e_ms, float(wl.bytes)], device=dev)
+    tot_bytes = float(wl.bytes) * world
     if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms_max = float(t.item())
-    h2d = wl.staging.numel() + wl.scores_host.numel() * 4
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        b = torch.tensor([float(wl.bytes)], device=dev)
+        dist.all_reduce(b, op=dist.ReduceOp.SUM)
+        tot_bytes = float(b.item())
+    e2e_ms_max = float(t[0].item())
+    h2d = wl.staging.numel() + (0 if tp else wl.scores_host.numel() * 4)
     d2h = out_idx.numel() * 4 + out_slot.numel() * 8 + out_cnt.numel() * 4
 
     if rank == 0:
@@ -341,27 +419,30 @@ def run_ours(args):
         kern_avg_ms = sum(kern_ms) / len(kern_ms)
         achieved = wl.bytes / (kern_avg_ms * 1e-3) / 1e9
         traffic = None
-        tp = ROOT / "profiles" / "traffic.json"
-        if tp.exists():
-            traffic = json.loads(tp.read_text()).get("rerotate_scatter_kernel_bytes_per_launch")
-        value = world * wl.bytes * args.steps / (ms_max * 1e-3) / 1e9
+        tp_file = ROOT / "profiles" / "traffic.json"
+        if tp_file.exists() and args.config == 2:
+            traffic = json.loads(tp_file.read_text()).get("rerotate_scatter_kernel_bytes_per_launch")
+        value = tot_bytes * args.steps / (ms_max * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama3-8b-8k-prompt", "layers": CFG["layers"], "kv_heads": CFG["kv_heads"],
-                       "head_dim": CFG["head_dim"], "block_size": CFG["block_size"], "tokens": CFG["tokens"],
-                       "chunks": CFG["tokens"] // CFG["chunk"], "rope": "flexible", "theta": CFG["theta"],
-                       "select": "top15%/layer", "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (1 GiB staging + 1.2 GiB paged cache per GPU), no flush"},
-            "us_per_prompt": round(ms_max / args.steps * 1e3, 2),
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg["name"], "layers": cfg["layers"], "kv_heads": cfg["kv_heads"],
+                       "kv_heads_per_gpu": wl.heads, "head_dim": cfg["head_dim"], "block_size": cfg["block_size"],
+                       "tokens_per_gpu": wl.tokens, "chunks": len(wl.chunk_len), "rope": "flexible",
+                       "theta": cfg["theta"], "select": f"top{int(cfg['ratio'] * 100)}%/layer/request",
+                       "scores": cfg["scores"] + (" (NCCL all-reduce over KV-head shards)" if tp else ""),
+                       "parallelism": (f"tp{world}" if tp else f"dp{world}"),
+                       "l2": "inputs larger than L2 (staging + paged cache >> 126 MB), no flush"},
+            "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config != 3 else None,
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "rotate_scatter_kernel", "peak_kind": peak_kind,
+                         "kernel": "bulk_pages_kernel (fused re-rotate + scatter)", "peak_kind": peak_kind,
                          "kernel_us": round(kern_avg_ms * 1e3, 2),
+                         "kernel_us_min": round(min(kern_ms) * 1e3, 2),
                          "algorithmic_bytes_per_launch": wl.bytes},
-            "e2e": {"value": round(world * wl.bytes * e2e_steps / (e2e_ms_max * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "e2e": {"value": round(tot_bytes * e2e_steps / (e2e_ms_max * 1e-3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms_max / e2e_steps, 4)},
             "gpu_launches": 3 * args.steps,
@@ -369,7 +450,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "device_errors": errors,
         }
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and args.config == 2 and not args.no_cpu_baseline:
             sys.path.insert(0, str(ROOT))
             cw, cbytes = make_cpu_workload(wl, chunks=args.cpu_chunks)
             reps, el = cpu_baseline_run(cw)
@@ -391,6 +472,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-chunks", type=int, default=4)
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2,
+                    help="BASELINE.json config: 2 (default, 8K prompt), 3 (64-request batch), 4 (70B, TP heads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
