@@ -126,7 +126,8 @@ __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kre
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
   const int per_tok = L.half_rot / 2;
   const uint32_t base = smem_addr(kreg);
-  for (int b0 = tid; b0 < ntask; b0 += U * nthreads) {
+  // warp-uniform trip count (score_add shuffles across the warp)
+  for (int b0 = tid; b0 - (tid & 31) < ntask; b0 += U * nthreads) {
     uint4 lo[U], hi[U];
     int off[U], slot[U], c[U];
 #pragma unroll
@@ -146,14 +147,15 @@ __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kre
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (off[u] < 0) continue;
-      const float4* q = fac + slot[u] * per_tok + c[u];
       float dv = 0.f;
-      if (NEOX) rotate_neox_q<E, SCORE>(q, L.pair_vecs, lo[u], hi[u], dv);
-      else rotate_gptj_q<E, SCORE>(q, L.pair_vecs, lo[u], dv);
-      if (SCORE) atomicAdd(&tok_dev[slot[u]], dv);
-      sts128(base + off[u], lo[u]);
-      if (NEOX) sts128(base + off[u] + hi_off, hi[u]);
+      if (off[u] >= 0) {
+        const float4* q = fac + slot[u] * per_tok + c[u];
+        if (NEOX) rotate_neox_q<E, SCORE>(q, L.pair_vecs, lo[u], hi[u], dv);
+        else rotate_gptj_q<E, SCORE>(q, L.pair_vecs, lo[u], dv);
+        sts128(base + off[u], lo[u]);
+        if (NEOX) sts128(base + off[u] + hi_off, hi[u]);
+      }
+      if (SCORE) score_add(tok_dev, off[u] >= 0 ? slot[u] : -1, dv);
     }
   }
 }

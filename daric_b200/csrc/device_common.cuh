@@ -226,6 +226,22 @@ __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, 
   }
 }
 
+// Adds each lane's deviation `v` to dev[slot] (slot < 0: nothing). When the
+// whole warp works on one slot (a warp's tasks are usually heads of one
+// token) the warp sums first and one lane adds; otherwise every lane adds.
+// Must be called by all 32 lanes of the warp.
+__device__ __forceinline__ void score_add(float* dev, int slot, float v) {
+  const unsigned full = 0xffffffffu;
+  const int s0 = __shfl_sync(full, slot, 0);
+  if (__all_sync(full, slot == s0)) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(full, v, o);
+    if ((threadIdx.x & 31) == 0 && s0 >= 0) atomicAdd(&dev[s0], v);
+  } else if (slot >= 0) {
+    atomicAdd(&dev[slot], v);
+  }
+}
+
 // Token slot of K row `row` of a page region.
 __device__ __forceinline__ int row_slot(const LayerDev& L, int row) {
   const uint32_t q = fdiv((uint32_t)row, L.tok_div);

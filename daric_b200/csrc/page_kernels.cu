@@ -140,7 +140,8 @@ __device__ __forceinline__ void rotate_rows_global(const LayerDev& L, const uint
   const int ntask = L.nrows * L.pair_vecs;
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
   const int per_tok = L.half_rot / 2;
-  for (int base = threadIdx.x; base < ntask; base += U * blockDim.x) {
+  // warp-uniform trip count (score_add shuffles across the warp)
+  for (int base = threadIdx.x; base - (int)(threadIdx.x & 31) < ntask; base += U * blockDim.x) {
     uint4 lo[U], hi[U];
     int off[U], slot[U], c[U];
 #pragma unroll
@@ -158,16 +159,18 @@ __device__ __forceinline__ void rotate_rows_global(const LayerDev& L, const uint
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      if (off[u] < 0) continue;
-      if (tok0 + slot[u] < len) {
+      float dv = 0.f;
+      const bool rot = off[u] >= 0 && tok0 + slot[u] < len;
+      if (rot) {
         const float4* q = fac_page + (int64_t)slot[u] * per_tok + c[u];
-        float dv = 0.f;
         if (NEOX) rotate_neox_q<E, SCORE>(q, L.pair_vecs, lo[u], hi[u], dv);
         else rotate_gptj_q<E, SCORE>(q, L.pair_vecs, lo[u], dv);
-        if (SCORE) atomicAdd(&tok_dev[slot[u]], dv);
       }
-      st_stream(dst + off[u], lo[u]);
-      if (NEOX) st_stream(dst + off[u] + hi_off, hi[u]);
+      if (off[u] >= 0) {
+        st_stream(dst + off[u], lo[u]);
+        if (NEOX) st_stream(dst + off[u] + hi_off, hi[u]);
+      }
+      if (SCORE) score_add(tok_dev, rot ? slot[u] : -1, dv);
     }
   }
 }

@@ -78,5 +78,6 @@ def test_sampled_pages_match_oracle(loaded):
         if wl.old_pos[m] != wl.new_pos[m]:
             R.rotate_tokens(layer, rot, np.arange(16), c, s)
         blk = wl.chunk_blocks[m][pg]
-        got = wl.kv[wl.names[l]][:, blk].contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+        name = wl.plan.layer_names[j]  # the store orders layers by sorted name
+        got = wl.kv[name][:, blk].contiguous().view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
         np.testing.assert_array_equal(got, layer.raw)
