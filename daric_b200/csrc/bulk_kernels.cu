@@ -28,11 +28,17 @@ constexpr int kBulkThreads = kConsumerWarps * 32 + 32;  // + one producer warp
 constexpr int kMaxStages = 8;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
-struct StageMeta {  // 24 bytes; kMaxStages of them fit [128, kBulkHeader)
+struct StageMeta {  // what the producer recorded when it issued a stage's loads
   int64_t job;
   int64_t page_local;
   int32_t blk;
   int32_t skip;
+  uint8_t* dst[2];     // store destinations of the regions (nreg <= 2)
+  float* sout;         // score output of the page's first slot (SCORE)
+  int32_t sn;          // slots with a score to write
+  int32_t nreg;        // regions (prefix entries) of the page
+  int32_t rbytes;      // bytes per region
+  int32_t pad;
 };
 static_assert(128 + kMaxStages * sizeof(StageMeta) <= kBulkHeader, "stage meta exceeds the header");
 
@@ -213,87 +219,161 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   __syncthreads();
 
   if (producer) {
-    if (lane != 0) return;
-    int64_t pj = find_job(p.jobs, p.num_jobs, ubeg);
-    auto issue = [&](int64_t i) {  // loads of unit ubeg+i into stage i % NS
-      const int s = (int)(i % NS);
-      const int64_t u = ubeg + i;
-      while (pj + 1 < p.num_jobs && p.jobs[pj + 1].unit_begin <= u) ++pj;
-      const JobDev j = p.jobs[pj];
-      const LayerDev& L = p.layers[j.layer];
-      const int64_t pl = u - j.unit_begin;
-      const int32_t blk = __ldg(&p.indices[j.idx_off + pl]);
-      int skip = blk == 0;
-      if (!skip && (blk < 0 || blk >= L.num_pages)) {
-        atomicOr(p.err, DEV_ERR_BLOCK_RANGE);
-        skip = 1;
+    // The producer warp prefetches the copy plan of 32 units at a time (one
+    // unit per lane: job lookup, block id, addresses) so that lane 0, which
+    // issues every bulk copy, never waits on a descriptor load.
+    const unsigned FULL = 0xffffffffu;
+    int64_t jc = find_job(p.jobs, p.num_jobs, ubeg);
+    int64_t batch = -1;
+    const uint8_t *my_src0 = nullptr, *my_src1 = nullptr;
+    uint8_t *my_dst0 = nullptr, *my_dst1 = nullptr;
+    const float4* my_fac = nullptr;
+    float* my_sout = nullptr;
+    int64_t my_job = 0, my_pl = 0;
+    int32_t my_blk = 0, my_skip = 1, my_nreg = 0, my_rb = 0, my_fb = 0, my_sn = 0;
+    auto prefetch = [&](int64_t b) {  // all lanes
+      const int64_t i = b * 32 + lane;
+      int64_t j = jc;
+      my_skip = 1;
+      my_nreg = 0;
+      my_fb = 0;
+      my_sn = 0;
+      if (i < n) {
+        const int64_t u = ubeg + i;
+        while (j + 1 < p.num_jobs && p.jobs[j + 1].unit_begin <= u) ++j;
+        const JobDev jd = p.jobs[j];
+        const LayerDev& L = p.layers[jd.layer];
+        const int64_t pl = u - jd.unit_begin;
+        const int32_t blk = __ldg(&p.indices[jd.idx_off + pl]);
+        int skip = blk == 0;
+        if (!skip && (blk < 0 || blk >= L.num_pages)) {
+          atomicOr(p.err, DEV_ERR_BLOCK_RANGE);
+          skip = 1;
+        }
+        my_job = j;
+        my_pl = pl;
+        my_blk = blk;
+        my_skip = skip;
+        my_nreg = L.prefix_size;
+        my_rb = (int32_t)L.suffix;
+        if (!skip && L.prefix_size <= 2) {
+          my_src0 = region_src(jd, L, pl, blk, 0);
+          my_dst0 = region_dst(jd, L, pl, blk, 0);
+          if (L.prefix_size == 2) {
+            my_src1 = region_src(jd, L, pl, blk, 1);
+            my_dst1 = region_dst(jd, L, pl, blk, 1);
+          }
+        }
+        if (!skip && unit_rotates(jd, L)) {
+          my_fb = (int32_t)page_factor_bytes(L.page_size, L.half_rot);
+          my_fac = p.fac + (jd.fac_tok + pl * L.page_size) * (L.half_rot / 2);
+        }
+        if (SCORE && jd.score_row >= 0 && jd.meta >= 0) {
+          const MetaDev m = p.metas[jd.meta];
+          const int64_t tok0 = pl * L.page_size;
+          const int64_t left = m.len - tok0;
+          my_sn = (int32_t)(left < 0 ? 0 : (left < L.page_size ? left : L.page_size));
+          my_sout = p.scores + (int64_t)jd.score_row * p.score_ld + m.score_col + tok0;
+        }
       }
-      meta[s] = StageMeta{pj, pl, blk, skip};
-      if (skip) {
+      jc = __shfl_sync(FULL, j, 31);
+    };
+    // loads of unit i into stage i % NS (warp-synchronous: every lane calls)
+    auto issue = [&](int64_t i) {
+      const int64_t b = i / 32;
+      if (b != batch) {
+        prefetch(b);
+        batch = b;
+      }
+      const int k = (int)(i - b * 32);
+      StageMeta st;
+      st.job = __shfl_sync(FULL, my_job, k);
+      st.page_local = __shfl_sync(FULL, my_pl, k);
+      st.blk = __shfl_sync(FULL, my_blk, k);
+      st.skip = __shfl_sync(FULL, my_skip, k);
+      st.nreg = __shfl_sync(FULL, my_nreg, k);
+      st.rbytes = __shfl_sync(FULL, my_rb, k);
+      st.sn = __shfl_sync(FULL, my_sn, k);
+      st.dst[0] = (uint8_t*)__shfl_sync(FULL, (unsigned long long)my_dst0, k);
+      st.dst[1] = (uint8_t*)__shfl_sync(FULL, (unsigned long long)my_dst1, k);
+      st.sout = (float*)__shfl_sync(FULL, (unsigned long long)my_sout, k);
+      const uint8_t* src0 = (const uint8_t*)__shfl_sync(FULL, (unsigned long long)my_src0, k);
+      const uint8_t* src1 = (const uint8_t*)__shfl_sync(FULL, (unsigned long long)my_src1, k);
+      const float4* fac = (const float4*)__shfl_sync(FULL, (unsigned long long)my_fac, k);
+      const uint32_t fb = (uint32_t)__shfl_sync(FULL, my_fb, k);
+      if (lane != 0) return;
+      const int s = (int)(i % NS);
+      meta[s] = st;
+      if (st.skip) {
         mbar_arrive(&full[s]);
         return;
       }
       uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-      const bool rot = unit_rotates(j, L);
-      const uint32_t fbytes = rot ? (uint32_t)page_factor_bytes(L.page_size, L.half_rot) : 0u;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(L.prefix_size * L.suffix) + fbytes);
-      for (int pf = 0; pf < L.prefix_size; ++pf)
-        bulk_load(buf + (size_t)pf * L.suffix, region_src(j, L, pl, blk, pf), (uint32_t)L.suffix, &full[s]);
-      if (rot)
-        bulk_load(buf + g.fac_off, p.fac + (j.fac_tok + pl * L.page_size) * (L.half_rot / 2), fbytes, &full[s]);
+      mbar_arrive_expect_tx(&full[s], (uint32_t)(st.nreg * st.rbytes) + fb);
+      if (st.nreg <= 2) {
+        bulk_load(buf, src0, (uint32_t)st.rbytes, &full[s]);
+        if (st.nreg == 2) bulk_load(buf + st.rbytes, src1, (uint32_t)st.rbytes, &full[s]);
+      } else {  // more than two regions per page: addresses computed here
+        const JobDev jd = p.jobs[st.job];
+        const LayerDev& L = p.layers[jd.layer];
+        for (int pf = 0; pf < st.nreg; ++pf)
+          bulk_load(buf + (size_t)pf * st.rbytes, region_src(jd, L, st.page_local, st.blk, pf),
+                    (uint32_t)st.rbytes, &full[s]);
+      }
+      if (fb) bulk_load(buf + g.fac_off, fac, fb, &full[s]);
     };
     int64_t issued = 0;
     for (; issued < NS - 1 && issued < n; ++issued) issue(issued);
-    bool prev_stored = false;  // unit i-1 has a pending store group
+    bool prev_stored = false;  // unit i-1 has a pending store group (lane 0)
     int64_t i = 0;
     for (; i < n; ++i) {
       const int s = (int)(i % NS);
-      if (!mbar_wait(&empty[s], (uint32_t)((i / NS) & 1))) {
-        atomicOr(p.err, DEV_ERR_TIMEOUT);
+      const bool ok = mbar_wait(&empty[s], (uint32_t)((i / NS) & 1));
+      if (__any_sync(FULL, !ok)) {
+        if (lane == 0) atomicOr(p.err, DEV_ERR_TIMEOUT);
         break;
       }
       const StageMeta st = meta[s];
-      bool stored = false;
-      if (!st.skip) {
-        const JobDev j = p.jobs[st.job];
-        const LayerDev& L = p.layers[j.layer];
+      const bool stored = !st.skip;
+      if (lane == 0 && stored) {
         uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-        for (int pf = 0; pf < L.prefix_size; ++pf)
-          bulk_store(region_dst(j, L, st.page_local, st.blk, pf), buf + (size_t)pf * L.suffix,
-                     (uint32_t)L.suffix);
-        bulk_commit();
-        stored = true;
-      }
-      if (SCORE) {
-        const JobDev j = p.jobs[st.job];
-        if (j.score_row >= 0 && j.meta >= 0) {
-          const LayerDev& L = p.layers[j.layer];
-          const MetaDev m = p.metas[j.meta];
-          const int64_t tok0 = st.page_local * L.page_size;
-          float* out = p.scores + (int64_t)j.score_row * p.score_ld + m.score_col + tok0;
-          float* dv = devs + s * dev_stride;
-          for (int q = 0; q < L.page_size; ++q) {
-            if (tok0 + q < m.len) out[q] = dv[q];
-            dv[q] = 0.f;
-          }
+        if (st.nreg <= 2) {
+          bulk_store(st.dst[0], buf, (uint32_t)st.rbytes);
+          if (st.nreg == 2) bulk_store(st.dst[1], buf + st.rbytes, (uint32_t)st.rbytes);
+        } else {
+          const JobDev jd = p.jobs[st.job];
+          const LayerDev& L = p.layers[jd.layer];
+          for (int pf = 0; pf < st.nreg; ++pf)
+            bulk_store(region_dst(jd, L, st.page_local, st.blk, pf), buf + (size_t)pf * st.rbytes,
+                       (uint32_t)st.rbytes);
         }
+        bulk_commit();
       }
+      if (SCORE && st.sn > 0) {
+        float* dv = devs + s * dev_stride;
+        for (int q = lane; q < st.sn; q += 32) st.sout[q] = dv[q];
+      }
+      if (SCORE)
+        for (int q = lane; q < dev_stride; q += 32) devs[s * dev_stride + q] = 0.f;
+      __syncwarp();
       // the next load goes into the stage of unit i-1: its stores must have
       // read it (unit i's group, committed last, may still be pending)
       if (issued < n) {
-        if (prev_stored) {
+        if (lane == 0 && prev_stored) {
           if (stored) bulk_wait_read<1>(); else bulk_wait_read<0>();
         }
+        __syncwarp();
         issue(issued);
         ++issued;
       }
       prev_stored = stored;
+      __syncwarp();
     }
-    if (i < n) {
+    if (i < n && lane == 0) {
       // timed out: drain the loads still in flight into this CTA's stages
       for (int64_t k = i + 1; k < issued; ++k) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
     }
-    bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
     return;
   }
 

@@ -238,7 +238,7 @@ struct BulkGeom {
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
-constexpr int kBulkHeader = 512;
+constexpr int kBulkHeader = 1024;
 
 inline size_t bulk_smem_bytes(const BulkGeom& g) {
   return kBulkHeader + (size_t)g.dev_bytes + (size_t)g.nstage * g.stage_bytes;
