@@ -65,15 +65,26 @@ struct DeviceGuard {
 // ------------------------------------------------------ per-device state --
 constexpr int kRingSlots = 16;
 
+constexpr size_t kSlotBytes = 1024 * 1024;  // pre-allocated descriptor bytes per ring slot
+
 struct RingSlot {
   std::mutex mu;
   uint8_t* host = nullptr;
   uint8_t* dev = nullptr;
   size_t cap = 0;
-  uint8_t* scratch = nullptr;  // device scratch of the call (rotary factors)
-  size_t scratch_cap = 0;
   cudaEvent_t done = nullptr;
   bool pending = false;
+};
+
+// Device scratch of the rotating calls (rotary factors), one per device.
+// A call waits on the GPU for the previous user (event) before writing it,
+// so calls on different streams stay ordered without blocking the host.
+struct Scratch {
+  std::mutex mu;
+  uint8_t* ptr = nullptr;
+  size_t cap = 0;
+  cudaEvent_t last = nullptr;
+  bool used = false;
 };
 
 struct DeviceCtx {
@@ -84,6 +95,7 @@ struct DeviceCtx {
   std::mutex mu;
   unsigned next = 0;
   RingSlot slots[kRingSlots];
+  Scratch scratch;
 };
 
 std::mutex g_ctx_mu;
@@ -100,7 +112,14 @@ DeviceCtx& device_ctx(int device) {
   DeviceGuard dg(device);
   DARIC_CUDA(cudaMalloc(&c->err_word, sizeof(int)));
   DARIC_CUDA(cudaMemset(c->err_word, 0, sizeof(int)));
-  for (auto& s : c->slots) DARIC_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+  for (auto& s : c->slots) {
+    // all slots up front, so the first calls after start-up allocate nothing
+    DARIC_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+    DARIC_CUDA(cudaHostAlloc((void**)&s.host, kSlotBytes, cudaHostAllocDefault));
+    DARIC_CUDA(cudaMalloc((void**)&s.dev, kSlotBytes));
+    s.cap = kSlotBytes;
+  }
+  DARIC_CUDA(cudaEventCreateWithFlags(&c->scratch.last, cudaEventDisableTiming));
   auto& ref = *c;
   g_ctx[device] = std::move(c);
   return ref;
@@ -134,18 +153,6 @@ class Upload {
   }
   uint8_t* host() { return slot_->host; }
   uint8_t* dev() { return slot_->dev; }
-  // Device scratch owned by this slot until finish(); grown on demand.
-  uint8_t* scratch(size_t bytes) {
-    if (slot_->scratch_cap < bytes) {
-      if (slot_->scratch) DARIC_CUDA(cudaFree(slot_->scratch));
-      slot_->scratch = nullptr;
-      slot_->scratch_cap = 0;
-      const size_t cap = std::max(bytes, slot_->scratch_cap * 2);
-      DARIC_CUDA(cudaMalloc((void**)&slot_->scratch, cap));
-      slot_->scratch_cap = cap;
-    }
-    return slot_->scratch;
-  }
   void send(size_t bytes, cudaStream_t s) {
     if (bytes) DARIC_CUDA(cudaMemcpyAsync(slot_->dev, slot_->host, bytes, cudaMemcpyHostToDevice, s));
   }
@@ -157,6 +164,37 @@ class Upload {
  private:
   RingSlot* slot_ = nullptr;
   std::unique_lock<std::mutex> lock_;
+};
+
+// Holds the device scratch for one call: the stream first waits (on the GPU)
+// for the scratch's previous user; release() marks this call as the user.
+// Growth (rare: a larger call than any before) waits on the host and
+// reallocates.
+class ScratchLease {
+ public:
+  ScratchLease(DeviceCtx& c, size_t bytes, cudaStream_t s) : sc_(c.scratch), lock_(c.scratch.mu), s_(s) {
+    if (sc_.cap < bytes) {
+      if (sc_.used) DARIC_CUDA(cudaEventSynchronize(sc_.last));
+      if (sc_.ptr) DARIC_CUDA(cudaFree(sc_.ptr));
+      sc_.ptr = nullptr;
+      const size_t cap = std::max(bytes, sc_.cap * 2);
+      sc_.cap = 0;
+      DARIC_CUDA(cudaMalloc((void**)&sc_.ptr, cap));
+      sc_.cap = cap;
+    } else if (sc_.used) {
+      DARIC_CUDA(cudaStreamWaitEvent(s, sc_.last, 0));
+    }
+  }
+  uint8_t* ptr() const { return sc_.ptr; }
+  void release() {
+    DARIC_CUDA(cudaEventRecord(sc_.last, s_));
+    sc_.used = true;
+  }
+
+ private:
+  Scratch& sc_;
+  std::lock_guard<std::mutex> lock_;
+  cudaStream_t s_;
 };
 
 // Lays out [section 0 | section 1 | ...] with 16-byte aligned sections.
@@ -524,7 +562,9 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
   if (!metas.empty()) std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
   if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
-  float4* fac = fac_bytes > 0 ? reinterpret_cast<float4*>(up.scratch((size_t)fac_bytes)) : nullptr;
+  std::unique_ptr<ScratchLease> lease;
+  if (fac_bytes > 0) lease = std::make_unique<ScratchLease>(dc, (size_t)fac_bytes, stream);
+  float4* fac = lease ? reinterpret_cast<float4*>(lease->ptr()) : nullptr;
   up.send(b.size, stream);
   if (!runs.empty()) {
     FactorLaunch fl{};
@@ -561,6 +601,7 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   } else {
     launch_plain_pages(p, gather, jp.vec16, dc.sm_count, stream);
   }
+  if (lease) lease->release();
   up.finish(stream);
 }
 
@@ -930,7 +971,8 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
       std::memcpy(up.host() + o_l, ld.data(), ld.size() * sizeof(LayerDev));
       std::memcpy(up.host() + o_s, segs.data(), segs.size() * sizeof(SegDev));
       std::memcpy(up.host() + o_r, runs.data(), runs.size() * sizeof(FacJobDev));
-      float4* fac = reinterpret_cast<float4*>(up.scratch((size_t)tok * T0.half_rot * 8));
+      ScratchLease lease(dc, (size_t)tok * T0.half_rot * 8, (cudaStream_t)stream);
+      float4* fac = reinterpret_cast<float4*>(lease.ptr());
       up.send(b.size, (cudaStream_t)stream);
       FactorLaunch fl{};
       fl.jobs = reinterpret_cast<const FacJobDev*>(up.dev() + o_r);
@@ -953,6 +995,7 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
       p.fac = fac;
       launch_rotate_inplace(p, RotKey{L0.kv_dtype, grp[0]->tab_dtype, L0.neox}, dc.sm_count,
                             (cudaStream_t)stream);
+      lease.release();
       up.finish((cudaStream_t)stream);
     }
   });
