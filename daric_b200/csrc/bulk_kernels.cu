@@ -28,17 +28,24 @@ constexpr int kBulkThreads = kConsumerWarps * 32 + 32;  // + one producer warp
 constexpr int kMaxStages = 8;
 constexpr uint32_t kWaitLimit = 1u << 22;
 
+constexpr int kMaxPagesPerUnit = 8;
+
 struct StageMeta {  // what the producer recorded when it issued a stage's loads
   int64_t job;
-  int64_t page_local;
-  int32_t blk;
-  int32_t skip;
-  uint8_t* dst[2];     // store destinations of the regions (nreg <= 2)
-  float* sout;         // score output of the page's first slot (SCORE)
-  int32_t sn;          // slots with a score to write
-  int32_t nreg;        // regions (prefix entries) of the page
-  int32_t rbytes;      // bytes per region
+  uint8_t* base;          // layer data
+  int64_t stg_off;        // job's store offset
+  int64_t page_stride;
+  int64_t prefix_stride;
+  float* sout;            // score output of the unit's first token (SCORE)
+  int32_t pl0;            // first page (job-local) of the unit
+  int32_t npg;            // pages in the unit
+  int32_t skipmask;       // bit g: page g is not copied (block id 0 / out of range)
+  int32_t nreg;           // regions (prefix entries) per page
+  int32_t rbytes;         // bytes per region
+  int32_t n_sel;          // pages of the job
+  int32_t sn;             // tokens with a score to write
   int32_t pad;
+  int32_t blk[kMaxPagesPerUnit];
 };
 static_assert(128 + kMaxStages * sizeof(StageMeta) <= kBulkHeader, "stage meta exceeds the header");
 
@@ -121,33 +128,46 @@ __device__ __forceinline__ int64_t find_job(const JobDev* jobs, int64_t n, int64
   return lo;
 }
 
-// Rotates the K rows of one region held in shared memory (in place) with
-// the page's factor block (also in shared memory).
+// Rotates the K rows of the unit's pages held in shared memory (in place).
+// Task t of the unit -> page g, row, pair c; the factors come from the
+// factor buffer in global memory (L2/L1 resident, shared by the heads).
 template <class E, bool NEOX, bool SCORE>
-__device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kreg, const float4* fac,
-                                                 int64_t tok0, int64_t len, float* tok_dev, int tid,
-                                                 int nthreads) {
-  constexpr int U = 4;
-  const int ntask = L.nrows * L.pair_vecs;
+__device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* stage, int page_data,
+                                                 const StageMeta& st, const float4* fac_unit, int64_t len,
+                                                 float* tok_dev, int tid, int nthreads) {
+  constexpr int U = 2;
+  const int per_page = L.nrows * L.pair_vecs;
+  const int ntask = per_page * st.npg;
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
   const int per_tok = L.half_rot / 2;
-  const uint32_t base = smem_addr(kreg);
+  const int64_t tok_base = (int64_t)st.pl0 * L.page_size;
+  const uint32_t base = smem_addr(stage) + (uint32_t)L.k_prefix * (uint32_t)st.rbytes;
   // warp-uniform trip count (score_add shuffles across the warp)
   for (int b0 = tid; b0 - (tid & 31) < ntask; b0 += U * nthreads) {
     uint4 lo[U], hi[U];
-    int off[U], slot[U], c[U];
+    float4 q[U][E::kPerVec / 2 > 4 ? 8 : 4];
+    int off[U], slot[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int t = b0 + u * nthreads;
       off[u] = -1;
+      slot[u] = -1;
       if (t < ntask) {
-        const int row = (int)fdiv((uint32_t)t, L.pair_div);
-        c[u] = t - row * L.pair_vecs;
-        slot[u] = row_slot(L, row);
-        if (tok0 + slot[u] < len) {
-          off[u] = row * L.row_bytes + c[u] * 16;
+        const int g = (int)fdiv((uint32_t)t, L.page_div);
+        const int r = t - g * per_page;
+        const int row = (int)fdiv((uint32_t)r, L.pair_div);
+        const int c = r - row * L.pair_vecs;
+        const int sl = row_slot(L, row);
+        const int64_t tok = (int64_t)g * L.page_size + sl;  // unit token
+        if (!((st.skipmask >> g) & 1) && tok_base + tok < len) {
+          off[u] = g * page_data + row * L.row_bytes + c * 16;
+          slot[u] = (int)tok;
           lo[u] = lds128(base + off[u]);
           if (NEOX) hi[u] = lds128(base + off[u] + hi_off);
+          const float4* fq = fac_unit + tok * per_tok + c;
+          constexpr int NG = NEOX ? E::kPerVec / 2 : E::kPerVec / 4;
+#pragma unroll
+          for (int k = 0; k < NG; ++k) q[u][k] = __ldg(fq + k * L.pair_vecs);
         }
       }
     }
@@ -155,25 +175,24 @@ __device__ __forceinline__ void rotate_rows_smem(const LayerDev& L, uint8_t* kre
     for (int u = 0; u < U; ++u) {
       float dv = 0.f;
       if (off[u] >= 0) {
-        const float4* q = fac + slot[u] * per_tok + c[u];
-        if (NEOX) rotate_neox_q<E, SCORE>(q, L.pair_vecs, lo[u], hi[u], dv);
-        else rotate_gptj_q<E, SCORE>(q, L.pair_vecs, lo[u], dv);
+        if (NEOX) rotate_neox_q<E, SCORE>(q[u], 1, lo[u], hi[u], dv);
+        else rotate_gptj_q<E, SCORE>(q[u], 1, lo[u], dv);
         sts128(base + off[u], lo[u]);
         if (NEOX) sts128(base + off[u] + hi_off, hi[u]);
       }
-      if (SCORE) score_add(tok_dev, off[u] >= 0 ? slot[u] : -1, dv);
+      if (SCORE) score_add(tok_dev, slot[u], dv);
     }
   }
 }
 
 // Warp-specialised pipeline. Warps 0..kConsumerWarps-1 rotate; the last
-// warp's lane 0 is the producer: it issues the bulk loads of unit u into
-// stage u % NS (full[s] completes when the bytes land), waits until every
-// consumer warp has released the unit (empty[s]), issues the bulk stores,
-// and reuses the stage of the previous unit once its stores have read it.
-// Shared memory: [0,128) full/empty barriers | [128,512) stage meta |
-// per-stage deviation slots | stages (page data, then the page's factor
-// block at fac_off).
+// warp is the producer: its 32 lanes prefetch the copy plans of 32 units at
+// a time, and lane 0 issues the bulk loads of unit u into stage u % NS
+// (full[s] completes when the bytes land), waits until every consumer warp
+// has released the unit (empty[s]), issues the bulk stores, and reuses the
+// stage of the previous unit once its stores have read it.
+// Shared memory: [0,128) full/empty barriers | [128,kBulkHeader) stage meta |
+// per-stage deviation slots | stages (page g of a unit at g * page_data).
 template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE>
 __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch p, BulkGeom g) {
   using E = Elem<KVT>;
@@ -184,6 +203,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   float* devs = reinterpret_cast<float*>(smem + kBulkHeader);  // NS x dev_stride floats
   uint8_t* stages = smem + kBulkHeader + g.dev_bytes;
   const int NS = g.nstage;
+  const int G = g.pages_per_unit;
   const int dev_stride = g.dev_bytes / (4 * NS);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -195,16 +215,13 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   if (ubeg >= uend) return;
   const int64_t n = uend - ubeg;
 
-  auto region_src = [&](const JobDev& j, const LayerDev& L, int64_t pl, int32_t blk, int pf) -> const uint8_t* {
-    if (GATHER) return L.base + (int64_t)pf * L.prefix_stride + (int64_t)blk * L.page_stride;
-    return p.store + j.stg_off + ((int64_t)pf * j.n_sel + pl) * L.suffix;
+  // address of region pf of job-local page pl (block blk) on the source /
+  // destination side
+  auto store_region = [&](const StageMeta& st, int pl, int pf) -> uint8_t* {
+    return p.store_mut + st.stg_off + ((int64_t)pf * st.n_sel + pl) * st.rbytes;
   };
-  auto region_dst = [&](const JobDev& j, const LayerDev& L, int64_t pl, int32_t blk, int pf) -> uint8_t* {
-    if (GATHER) return p.store_mut + j.stg_off + ((int64_t)pf * j.n_sel + pl) * L.suffix;
-    return L.base + (int64_t)pf * L.prefix_stride + (int64_t)blk * L.page_stride;
-  };
-  auto unit_rotates = [&](const JobDev& j, const LayerDev& L) -> bool {
-    return ROTATE && j.meta >= 0 && L.has_rot && p.metas[j.meta].rotate;
+  auto layer_region = [&](const StageMeta& st, int32_t blk, int pf) -> uint8_t* {
+    return st.base + (int64_t)pf * st.prefix_stride + (int64_t)blk * st.page_stride;
   };
 
   if (tid == 0) {
@@ -219,64 +236,58 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   __syncthreads();
 
   if (producer) {
-    // The producer warp prefetches the copy plan of 32 units at a time (one
-    // unit per lane: job lookup, block id, addresses) so that lane 0, which
-    // issues every bulk copy, never waits on a descriptor load.
     const unsigned FULL = 0xffffffffu;
     int64_t jc = find_job(p.jobs, p.num_jobs, ubeg);
     int64_t batch = -1;
-    const uint8_t *my_src0 = nullptr, *my_src1 = nullptr;
-    uint8_t *my_dst0 = nullptr, *my_dst1 = nullptr;
-    const float4* my_fac = nullptr;
-    float* my_sout = nullptr;
-    int64_t my_job = 0, my_pl = 0;
-    int32_t my_blk = 0, my_skip = 1, my_nreg = 0, my_rb = 0, my_fb = 0, my_sn = 0;
+    // this lane's unit of the current batch
+    StageMeta mine{};
     auto prefetch = [&](int64_t b) {  // all lanes
       const int64_t i = b * 32 + lane;
       int64_t j = jc;
-      my_skip = 1;
-      my_nreg = 0;
-      my_fb = 0;
-      my_sn = 0;
+      mine.npg = 0;
+      mine.skipmask = 0;
+      mine.sn = 0;
       if (i < n) {
         const int64_t u = ubeg + i;
         while (j + 1 < p.num_jobs && p.jobs[j + 1].unit_begin <= u) ++j;
         const JobDev jd = p.jobs[j];
         const LayerDev& L = p.layers[jd.layer];
-        const int64_t pl = u - jd.unit_begin;
-        const int32_t blk = __ldg(&p.indices[jd.idx_off + pl]);
-        int skip = blk == 0;
-        if (!skip && (blk < 0 || blk >= L.num_pages)) {
-          atomicOr(p.err, DEV_ERR_BLOCK_RANGE);
-          skip = 1;
-        }
-        my_job = j;
-        my_pl = pl;
-        my_blk = blk;
-        my_skip = skip;
-        my_nreg = L.prefix_size;
-        my_rb = (int32_t)L.suffix;
-        if (!skip && L.prefix_size <= 2) {
-          my_src0 = region_src(jd, L, pl, blk, 0);
-          my_dst0 = region_dst(jd, L, pl, blk, 0);
-          if (L.prefix_size == 2) {
-            my_src1 = region_src(jd, L, pl, blk, 1);
-            my_dst1 = region_dst(jd, L, pl, blk, 1);
+        const int pl0 = (int)(u - jd.unit_begin) * G;
+        const int npg = min(G, jd.n_sel - pl0);
+        mine.job = j;
+        mine.base = L.base;
+        mine.stg_off = jd.stg_off;
+        mine.page_stride = L.page_stride;
+        mine.prefix_stride = L.prefix_stride;
+        mine.pl0 = pl0;
+        mine.npg = npg;
+        mine.nreg = L.prefix_size;
+        mine.rbytes = (int32_t)L.suffix;
+        mine.n_sel = jd.n_sel;
+        for (int q = 0; q < kMaxPagesPerUnit; ++q) {
+          if (q >= npg) break;
+          const int32_t blk = __ldg(&p.indices[jd.idx_off + pl0 + q]);
+          int skip = blk == 0;
+          if (!skip && (blk < 0 || blk >= L.num_pages)) {
+            atomicOr(p.err, DEV_ERR_BLOCK_RANGE);
+            skip = 1;
           }
-        }
-        if (!skip && unit_rotates(jd, L)) {
-          my_fb = (int32_t)page_factor_bytes(L.page_size, L.half_rot);
-          my_fac = p.fac + (jd.fac_tok + pl * L.page_size) * (L.half_rot / 2);
+          mine.blk[q] = blk;
+          mine.skipmask |= skip << q;
         }
         if (SCORE && jd.score_row >= 0 && jd.meta >= 0) {
           const MetaDev m = p.metas[jd.meta];
-          const int64_t tok0 = pl * L.page_size;
+          const int64_t tok0 = (int64_t)pl0 * L.page_size;
           const int64_t left = m.len - tok0;
-          my_sn = (int32_t)(left < 0 ? 0 : (left < L.page_size ? left : L.page_size));
-          my_sout = p.scores + (int64_t)jd.score_row * p.score_ld + m.score_col + tok0;
+          const int64_t cap = (int64_t)npg * L.page_size;
+          mine.sn = (int32_t)(left < 0 ? 0 : (left < cap ? left : cap));
+          mine.sout = p.scores + (int64_t)jd.score_row * p.score_ld + m.score_col + tok0;
         }
       }
       jc = __shfl_sync(FULL, j, 31);
+    };
+    auto shfl64 = [&](auto v, int k) {
+      return (decltype(v))__shfl_sync(FULL, (unsigned long long)v, k);
     };
     // loads of unit i into stage i % NS (warp-synchronous: every lane calls)
     auto issue = [&](int64_t i) {
@@ -287,40 +298,39 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       }
       const int k = (int)(i - b * 32);
       StageMeta st;
-      st.job = __shfl_sync(FULL, my_job, k);
-      st.page_local = __shfl_sync(FULL, my_pl, k);
-      st.blk = __shfl_sync(FULL, my_blk, k);
-      st.skip = __shfl_sync(FULL, my_skip, k);
-      st.nreg = __shfl_sync(FULL, my_nreg, k);
-      st.rbytes = __shfl_sync(FULL, my_rb, k);
-      st.sn = __shfl_sync(FULL, my_sn, k);
-      st.dst[0] = (uint8_t*)__shfl_sync(FULL, (unsigned long long)my_dst0, k);
-      st.dst[1] = (uint8_t*)__shfl_sync(FULL, (unsigned long long)my_dst1, k);
-      st.sout = (float*)__shfl_sync(FULL, (unsigned long long)my_sout, k);
-      const uint8_t* src0 = (const uint8_t*)__shfl_sync(FULL, (unsigned long long)my_src0, k);
-      const uint8_t* src1 = (const uint8_t*)__shfl_sync(FULL, (unsigned long long)my_src1, k);
-      const float4* fac = (const float4*)__shfl_sync(FULL, (unsigned long long)my_fac, k);
-      const uint32_t fb = (uint32_t)__shfl_sync(FULL, my_fb, k);
+      st.job = __shfl_sync(FULL, mine.job, k);
+      st.base = shfl64(mine.base, k);
+      st.stg_off = __shfl_sync(FULL, mine.stg_off, k);
+      st.page_stride = __shfl_sync(FULL, mine.page_stride, k);
+      st.prefix_stride = __shfl_sync(FULL, mine.prefix_stride, k);
+      st.sout = shfl64(mine.sout, k);
+      st.pl0 = __shfl_sync(FULL, mine.pl0, k);
+      st.npg = __shfl_sync(FULL, mine.npg, k);
+      st.skipmask = __shfl_sync(FULL, mine.skipmask, k);
+      st.nreg = __shfl_sync(FULL, mine.nreg, k);
+      st.rbytes = __shfl_sync(FULL, mine.rbytes, k);
+      st.n_sel = __shfl_sync(FULL, mine.n_sel, k);
+      st.sn = __shfl_sync(FULL, mine.sn, k);
+      st.pad = 0;
+#pragma unroll
+      for (int q = 0; q < kMaxPagesPerUnit; ++q) st.blk[q] = __shfl_sync(FULL, mine.blk[q], k);
       if (lane != 0) return;
       const int s = (int)(i % NS);
       meta[s] = st;
-      if (st.skip) {
+      const int live = st.npg - __popc(st.skipmask);
+      if (live == 0) {
         mbar_arrive(&full[s]);
         return;
       }
       uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(st.nreg * st.rbytes) + fb);
-      if (st.nreg <= 2) {
-        bulk_load(buf, src0, (uint32_t)st.rbytes, &full[s]);
-        if (st.nreg == 2) bulk_load(buf + st.rbytes, src1, (uint32_t)st.rbytes, &full[s]);
-      } else {  // more than two regions per page: addresses computed here
-        const JobDev jd = p.jobs[st.job];
-        const LayerDev& L = p.layers[jd.layer];
-        for (int pf = 0; pf < st.nreg; ++pf)
-          bulk_load(buf + (size_t)pf * st.rbytes, region_src(jd, L, st.page_local, st.blk, pf),
-                    (uint32_t)st.rbytes, &full[s]);
+      mbar_arrive_expect_tx(&full[s], (uint32_t)(live * st.nreg * st.rbytes));
+      for (int q = 0; q < st.npg; ++q) {
+        if ((st.skipmask >> q) & 1) continue;
+        for (int pf = 0; pf < st.nreg; ++pf) {
+          const uint8_t* src = GATHER ? layer_region(st, st.blk[q], pf) : store_region(st, st.pl0 + q, pf);
+          bulk_load(buf + (size_t)q * g.page_data + (size_t)pf * st.rbytes, src, (uint32_t)st.rbytes, &full[s]);
+        }
       }
-      if (fb) bulk_load(buf + g.fac_off, fac, fb, &full[s]);
     };
     int64_t issued = 0;
     for (; issued < NS - 1 && issued < n; ++issued) issue(issued);
@@ -333,28 +343,25 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
         if (lane == 0) atomicOr(p.err, DEV_ERR_TIMEOUT);
         break;
       }
-      const StageMeta st = meta[s];
-      const bool stored = !st.skip;
+      const StageMeta& st = meta[s];
+      const bool stored = st.npg > __popc(st.skipmask);
       if (lane == 0 && stored) {
         uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-        if (st.nreg <= 2) {
-          bulk_store(st.dst[0], buf, (uint32_t)st.rbytes);
-          if (st.nreg == 2) bulk_store(st.dst[1], buf + st.rbytes, (uint32_t)st.rbytes);
-        } else {
-          const JobDev jd = p.jobs[st.job];
-          const LayerDev& L = p.layers[jd.layer];
-          for (int pf = 0; pf < st.nreg; ++pf)
-            bulk_store(region_dst(jd, L, st.page_local, st.blk, pf), buf + (size_t)pf * st.rbytes,
-                       (uint32_t)st.rbytes);
+        for (int q = 0; q < st.npg; ++q) {
+          if ((st.skipmask >> q) & 1) continue;
+          for (int pf = 0; pf < st.nreg; ++pf) {
+            uint8_t* dst = GATHER ? store_region(st, st.pl0 + q, pf) : layer_region(st, st.blk[q], pf);
+            bulk_store(dst, buf + (size_t)q * g.page_data + (size_t)pf * st.rbytes, (uint32_t)st.rbytes);
+          }
         }
         bulk_commit();
       }
-      if (SCORE && st.sn > 0) {
+      if (SCORE) {
         float* dv = devs + s * dev_stride;
         for (int q = lane; q < st.sn; q += 32) st.sout[q] = dv[q];
+        __syncwarp();
+        for (int q = lane; q < dev_stride; q += 32) dv[q] = 0.f;
       }
-      if (SCORE)
-        for (int q = lane; q < dev_stride; q += 32) devs[s * dev_stride + q] = 0.f;
       __syncwarp();
       // the next load goes into the stage of unit i-1: its stores must have
       // read it (unit i's group, committed last, may still be pending)
@@ -384,17 +391,19 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       atomicOr(p.err, DEV_ERR_TIMEOUT);
       break;
     }
-    const StageMeta st = meta[s];
-    const JobDev j = p.jobs[st.job];
-    const LayerDev& L = p.layers[j.layer];
-    if (!st.skip && unit_rotates(j, L)) {
-      uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-      const int64_t len = p.metas[j.meta].len;
-      const int64_t tok0 = st.page_local * L.page_size;
-      rotate_rows_smem<E, NEOX, SCORE>(L, buf + (size_t)L.k_prefix * L.suffix,
-                                       reinterpret_cast<const float4*>(buf + g.fac_off), tok0, len,
-                                       devs + s * dev_stride, tid, kConsumers);
-      fence_proxy_async();
+    const StageMeta& st = meta[s];
+    if (ROTATE && st.npg > __popc(st.skipmask)) {
+      const JobDev j = p.jobs[st.job];
+      const LayerDev& L = p.layers[j.layer];
+      if (j.meta >= 0 && L.has_rot) {
+        const MetaDev m = p.metas[j.meta];
+        if (m.rotate) {
+          const float4* fac_unit = p.fac + (j.fac_tok + (int64_t)st.pl0 * L.page_size) * (L.half_rot / 2);
+          rotate_unit_smem<E, NEOX, SCORE>(L, stages + (size_t)s * g.stage_bytes, g.page_data, st, fac_unit,
+                                           m.len, devs + s * dev_stride, tid, kConsumers);
+          fence_proxy_async();
+        }
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);

@@ -433,30 +433,30 @@ bool bulk_pipeline_enabled() {
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Bulk pipeline geometry for a launch, or nstage = 0 when a unit (page data
-// plus, when rotating, its factor block) does not fit two stages.
-BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores) {
+// Bulk pipeline geometry for a launch, or nstage = 0 when the pipeline
+// cannot hold three stages (load, rotate and store in flight together).
+// Small pages are packed into units of up to 8 consecutive pages of a job so
+// that every unit carries about 64 KiB.
+BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool scores) {
   BulkGeom g{};
-  size_t data = 0, fac = 0, dev = 0;
+  size_t page = 0, slots = 0;
   for (const auto& l : layers) {
-    data = std::max(data, (size_t)l.prefix_size * (size_t)l.suffix);
-    if (rotate) fac = std::max(fac, page_factor_bytes(l.page_size, l.half_rot));
-    if (scores) dev = std::max(dev, (size_t)l.page_size * 4);
+    page = std::max(page, (size_t)l.prefix_size * (size_t)l.suffix);
+    slots = std::max(slots, (size_t)std::max(l.page_size, 1));
   }
-  const size_t fac_off = round_up(data, 128);
-  const size_t stage = round_up(fac_off + fac, 128);
-  if (data == 0 || data + fac >= (1u << 20)) return g;
-  // stages fill what is left after the header and one deviation slot array
-  // per stage
+  if (page == 0 || page >= (1u << 20)) return g;
+  const size_t per_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / page));
+  const size_t stage = round_up(per_unit * page, 128);
+  const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
   size_t ns = 0;
-  for (size_t k = 8; k >= 2; --k)
-    if (kBulkHeader + k * round_up(dev, 16) + 128 + k * stage <= (size_t)dc.smem_optin) { ns = k; break; }
-  if (ns < 2) return g;
-  dev = round_up(ns * round_up(dev, 16), 128);
+  for (size_t k = 8; k >= 3; --k)
+    if (kBulkHeader + round_up(k * dev, 128) + k * stage <= (size_t)dc.smem_optin) { ns = k; break; }
+  if (ns < 3) return g;
   g.nstage = (int32_t)ns;
   g.stage_bytes = (int32_t)stage;
-  g.fac_off = (int32_t)fac_off;
-  g.dev_bytes = (int32_t)dev;
+  g.pages_per_unit = (int32_t)per_unit;
+  g.page_data = (int32_t)page;
+  g.dev_bytes = (int32_t)round_up(ns * dev, 128);
   return g;
 }
 
@@ -476,7 +476,19 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   // Layer table restricted to this launch's layers.
   std::vector<int> slot_map(jp.uniq.size(), -1);
   std::vector<LayerDev> layers;
-  std::vector<const LayerHost*> lhost;
+  for (int64_t i : job_index) {
+    const int us = jp.layer_slot[i];
+    if (slot_map[us] < 0) {
+      slot_map[us] = (int)layers.size();
+      layers.push_back(base_layer_dev(*jp.uniq[us]));
+    }
+  }
+  // Kernel choice: the bulk pipeline (units of pages_per_unit pages) when
+  // jobs are 16-byte aligned and a unit fits three stages, else SIMT (units
+  // of one page).
+  const BulkGeom bg =
+      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate && scores) : BulkGeom{};
+  const int64_t upp = bg.nstage >= 3 ? bg.pages_per_unit : 1;
   std::vector<JobDev> jobs;
   jobs.reserve(job_index.size());
   // Factor runs: one per (rotating chunk, rotary table), padded to whole pages.
@@ -486,11 +498,6 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   int64_t units = 0;
   for (int64_t i : job_index) {
     const int us = jp.layer_slot[i];
-    if (slot_map[us] < 0) {
-      slot_map[us] = (int)layers.size();
-      layers.push_back(base_layer_dev(*jp.uniq[us]));
-      lhost.push_back(jp.uniq[us]);
-    }
     if (jp.n_sel[i] == 0) continue;
     JobDev j{};
     j.stg_off = offsets[i];
@@ -533,7 +540,7 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
       }
     }
     jobs.push_back(j);
-    units += jp.n_sel[i];
+    units += (jp.n_sel[i] + upp - 1) / upp;
   }
   if (units == 0) return;
   // token offsets and float4 item offsets of the runs
@@ -591,9 +598,7 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   p.score_ld = score_ld;
   p.err = dc.err_word;
   p.fac = fac;
-  const BulkGeom bg =
-      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate, rotate && scores) : BulkGeom{};
-  if (bg.nstage >= 2) {
+  if (bg.nstage >= 3) {
     if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
     else launch_bulk_plain(p, bg, gather, dc.sm_count, stream);
   } else if (rotate) {
@@ -695,6 +700,7 @@ void resolve_rotary(LayerHost& L, int kv_dtype, const void* table, int tab_dtype
   d.tok_mod = make_fastdiv((uint32_t)page_size);
   d.tail_vecs = d.row_vecs - d.rot_vecs;
   d.tail_div = make_fastdiv((uint32_t)(d.tail_vecs > 0 ? d.tail_vecs : 1));
+  d.page_div = make_fastdiv((uint32_t)(d.nrows * d.pair_vecs));
   d.half_rot = (int32_t)half;
   d.table = (const uint8_t*)table;
   d.table_row = rot_dim * tab_es;

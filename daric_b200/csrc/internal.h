@@ -90,6 +90,7 @@ struct LayerDev {
   FastDiv tok_div;        // row -> token (before the modulo)
   FastDiv tok_mod;        // modulo page_size
   FastDiv tail_div;       // row_vecs - rot_vecs (non-rotated vectors per row)
+  FastDiv page_div;       // nrows * pair_vecs (rotation tasks per page)
   int32_t tail_vecs;      // row_vecs - rot_vecs
   int32_t half_rot;       // rotary_dim / 2 (elements)
   const uint8_t* table;   // cos_sin_cache
@@ -228,17 +229,20 @@ enum : int {
 };
 
 // Geometry of the bulk-copy pipeline: NSTAGE shared-memory stages of
-// stage_bytes each (page data, then fac_off.. the page's factor block),
-// after a dev_bytes region of per-slot deviations.
+// stage_bytes each, after the header and a dev_bytes region of per-slot
+// deviations. A unit is up to pages_per_unit consecutive pages of one job;
+// page g of a unit occupies [g * page_data, (g + 1) * page_data) of its stage.
 struct BulkGeom {
   int32_t nstage;
   int32_t stage_bytes;
-  int32_t fac_off;    // offset of the factor block inside a stage
+  int32_t pages_per_unit;
+  int32_t page_data;
   int32_t dev_bytes;
+  int32_t pad;
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
-constexpr int kBulkHeader = 1024;
+constexpr int kBulkHeader = 2048;
 
 inline size_t bulk_smem_bytes(const BulkGeom& g) {
   return kBulkHeader + (size_t)g.dev_bytes + (size_t)g.nstage * g.stage_bytes;
