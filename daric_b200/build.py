@@ -43,7 +43,7 @@ def _compile(src: Path, obj: Path, extra: list[str]) -> None:
     cmd = [nvcc(), *ARCH, *_flags(), *extra, "-x", "cu" if src.suffix == ".cu" else "c++",
            "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cpp":
-        cmd = [nvcc(), *_flags(), *extra, "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc(), *ARCH, *_flags(), *extra, "-c", str(src), "-o", str(obj)]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stdout}\n{r.stderr}")

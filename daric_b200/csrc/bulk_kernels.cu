@@ -37,6 +37,7 @@ struct StageMeta {  // what the producer recorded when it issued a stage's loads
   int64_t page_stride;
   int64_t prefix_stride;
   float* sout;            // score output of the unit's first token (SCORE)
+  const float4* fac;      // factor block to stage with the pages (nullptr: none)
   int32_t pl0;            // first page (job-local) of the unit
   int32_t npg;            // pages in the unit
   int32_t skipmask;       // bit g: page g is not copied (block id 0 / out of range)
@@ -44,7 +45,7 @@ struct StageMeta {  // what the producer recorded when it issued a stage's loads
   int32_t rbytes;         // bytes per region
   int32_t n_sel;          // pages of the job
   int32_t sn;             // tokens with a score to write
-  int32_t pad;
+  int32_t fac_bytes;      // bytes of the staged factor block
   int32_t blk[kMaxPagesPerUnit];
 };
 static_assert(128 + kMaxStages * sizeof(StageMeta) <= kBulkHeader, "stage meta exceeds the header");
@@ -130,11 +131,12 @@ __device__ __forceinline__ int64_t find_job(const JobDev* jobs, int64_t n, int64
 
 // Rotates the K rows of the unit's pages held in shared memory (in place).
 // Task t of the unit -> page g, row, pair c; the factors come from the
-// factor buffer in global memory (L2/L1 resident, shared by the heads).
+// unit's factor block staged beside the pages (fac_staged) or straight from
+// the factor buffer in global memory (L2 resident, shared by the heads).
 template <class E, bool NEOX, bool SCORE>
 __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* stage, int page_data,
-                                                 const StageMeta& st, const float4* fac_unit, int64_t len,
-                                                 float* tok_dev, int tid, int nthreads) {
+                                                 const StageMeta& st, const float4* fac_unit, bool fac_staged,
+                                                 int64_t len, float* tok_dev, int tid, int nthreads) {
   constexpr int U = 2;
   const int per_page = L.nrows * L.pair_vecs;
   const int ntask = per_page * st.npg;
@@ -166,8 +168,18 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
           if (NEOX) hi[u] = lds128(base + off[u] + hi_off);
           const float4* fq = fac_unit + tok * per_tok + c;
           constexpr int NG = NEOX ? E::kPerVec / 2 : E::kPerVec / 4;
+          if (fac_staged) {
+            const uint32_t fa = smem_addr(fq);
 #pragma unroll
-          for (int k = 0; k < NG; ++k) q[u][k] = __ldg(fq + k * L.pair_vecs);
+            for (int k = 0; k < NG; ++k) {
+              const uint4 w = lds128(fa + (uint32_t)(k * L.pair_vecs) * 16u);
+              q[u][k] = make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z),
+                                    __uint_as_float(w.w));
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < NG; ++k) q[u][k] = __ldg(fq + k * L.pair_vecs);
+          }
         }
       }
     }
@@ -247,6 +259,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       mine.npg = 0;
       mine.skipmask = 0;
       mine.sn = 0;
+      mine.fac = nullptr;
+      mine.fac_bytes = 0;
       if (i < n) {
         const int64_t u = ubeg + i;
         while (j + 1 < p.num_jobs && p.jobs[j + 1].unit_begin <= u) ++j;
@@ -274,6 +288,11 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
           }
           mine.blk[q] = blk;
           mine.skipmask |= skip << q;
+        }
+        if (ROTATE && g.fac_off > 0 && jd.meta >= 0 && L.has_rot && p.metas[jd.meta].rotate) {
+          const int per_tok = L.half_rot / 2;
+          mine.fac = p.fac + (jd.fac_tok + (int64_t)pl0 * L.page_size) * per_tok;
+          mine.fac_bytes = (int32_t)((size_t)npg * page_factor_bytes(L.page_size, L.half_rot));
         }
         if (SCORE && jd.score_row >= 0 && jd.meta >= 0) {
           const MetaDev m = p.metas[jd.meta];
@@ -311,7 +330,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       st.rbytes = __shfl_sync(FULL, mine.rbytes, k);
       st.n_sel = __shfl_sync(FULL, mine.n_sel, k);
       st.sn = __shfl_sync(FULL, mine.sn, k);
-      st.pad = 0;
+      st.fac = shfl64(mine.fac, k);
+      st.fac_bytes = __shfl_sync(FULL, mine.fac_bytes, k);
 #pragma unroll
       for (int q = 0; q < kMaxPagesPerUnit; ++q) st.blk[q] = __shfl_sync(FULL, mine.blk[q], k);
       if (lane != 0) return;
@@ -323,7 +343,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
         return;
       }
       uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(live * st.nreg * st.rbytes));
+      const uint32_t fb = (uint32_t)st.fac_bytes;
+      mbar_arrive_expect_tx(&full[s], (uint32_t)(live * st.nreg * st.rbytes) + fb);
+      if (fb) bulk_load(buf + g.fac_off, st.fac, fb, &full[s]);
       for (int q = 0; q < st.npg; ++q) {
         if ((st.skipmask >> q) & 1) continue;
         for (int pf = 0; pf < st.nreg; ++pf) {
@@ -398,9 +420,13 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       if (j.meta >= 0 && L.has_rot) {
         const MetaDev m = p.metas[j.meta];
         if (m.rotate) {
-          const float4* fac_unit = p.fac + (j.fac_tok + (int64_t)st.pl0 * L.page_size) * (L.half_rot / 2);
-          rotate_unit_smem<E, NEOX, SCORE>(L, stages + (size_t)s * g.stage_bytes, g.page_data, st, fac_unit,
-                                           m.len, devs + s * dev_stride, tid, kConsumers);
+          uint8_t* stage = stages + (size_t)s * g.stage_bytes;
+          const bool staged = g.fac_off > 0;
+          const float4* fac_unit =
+              staged ? reinterpret_cast<const float4*>(stage + g.fac_off)
+                     : p.fac + (j.fac_tok + (int64_t)st.pl0 * L.page_size) * (L.half_rot / 2);
+          rotate_unit_smem<E, NEOX, SCORE>(L, stage, g.page_data, st, fac_unit, staged, m.len,
+                                           devs + s * dev_stride, tid, kConsumers);
           fence_proxy_async();
         }
       }

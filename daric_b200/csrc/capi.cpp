@@ -436,27 +436,50 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Bulk pipeline geometry for a launch, or nstage = 0 when the pipeline
 // cannot hold three stages (load, rotate and store in flight together).
 // Small pages are packed into units of up to 8 consecutive pages of a job so
-// that every unit carries about 64 KiB.
-BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool scores) {
+// that every unit carries about 64 KiB; the rotating units' factor block is
+// staged with the pages when three such stages still fit, else the consumer
+// warps read it from L2. DARIC_BULK_UNIT_PAGES / DARIC_BULK_FACTORS=l2 are
+// diagnostic overrides for A/B measurements.
+BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores) {
   BulkGeom g{};
-  size_t page = 0, slots = 0;
+  size_t page = 0, slots = 0, fac = 0;
   for (const auto& l : layers) {
     page = std::max(page, (size_t)l.prefix_size * (size_t)l.suffix);
     slots = std::max(slots, (size_t)std::max(l.page_size, 1));
+    if (rotate) fac = std::max(fac, page_factor_bytes(l.page_size, l.half_rot));
   }
   if (page == 0 || page >= (1u << 20)) return g;
-  const size_t per_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / page));
-  const size_t stage = round_up(per_unit * page, 128);
+  size_t per_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / page));
+  if (const char* v = std::getenv("DARIC_BULK_UNIT_PAGES")) {
+    const long want = std::strtol(v, nullptr, 10);
+    if (want >= 1 && want <= 8) per_unit = (size_t)want;
+  }
+  const char* fv = std::getenv("DARIC_BULK_FACTORS");
+  const bool allow_staged = !(fv && std::strcmp(fv, "l2") == 0);
+  auto stages_for = [&](size_t stage, size_t dev) -> size_t {
+    for (size_t k = 8; k >= 3; --k)
+      if (kBulkHeader + round_up(k * dev, 128) + k * stage <= (size_t)dc.smem_optin) return k;
+    return 0;
+  };
   const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
-  size_t ns = 0;
-  for (size_t k = 8; k >= 3; --k)
-    if (kBulkHeader + round_up(k * dev, 128) + k * stage <= (size_t)dc.smem_optin) { ns = k; break; }
+  const size_t data = round_up(per_unit * page, 128);
+  size_t stage = data, fac_off = 0, ns = 0;
+  if (fac > 0 && allow_staged) {
+    const size_t with = round_up(data + per_unit * fac, 128);
+    ns = stages_for(with, dev);
+    if (ns >= 3) {
+      stage = with;
+      fac_off = data;
+    }
+  }
+  if (fac_off == 0) ns = stages_for(stage, dev);
   if (ns < 3) return g;
   g.nstage = (int32_t)ns;
   g.stage_bytes = (int32_t)stage;
   g.pages_per_unit = (int32_t)per_unit;
   g.page_data = (int32_t)page;
   g.dev_bytes = (int32_t)round_up(ns * dev, 128);
+  g.fac_off = (int32_t)fac_off;
   return g;
 }
 
@@ -487,7 +510,7 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   // jobs are 16-byte aligned and a unit fits three stages, else SIMT (units
   // of one page).
   const BulkGeom bg =
-      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate && scores) : BulkGeom{};
+      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate, rotate && scores) : BulkGeom{};
   const int64_t upp = bg.nstage >= 3 ? bg.pages_per_unit : 1;
   std::vector<JobDev> jobs;
   jobs.reserve(job_index.size());

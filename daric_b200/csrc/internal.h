@@ -238,7 +238,7 @@ struct BulkGeom {
   int32_t pages_per_unit;
   int32_t page_data;
   int32_t dev_bytes;
-  int32_t pad;
+  int32_t fac_off;    // >0: the unit's factor block is staged at this offset; 0: read from L2
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
