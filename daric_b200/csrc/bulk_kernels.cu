@@ -37,7 +37,7 @@ struct StageMeta {  // what the producer recorded when it issued a stage's loads
   int64_t page_stride;
   int64_t prefix_stride;
   float* sout;            // score output of the unit's first token (SCORE)
-  const float4* fac;      // factor block to stage with the pages (nullptr: none)
+  const uint8_t* fac;     // factor block to stage with the pages (nullptr: none)
   int32_t pl0;            // first page (job-local) of the unit
   int32_t npg;            // pages in the unit
   int32_t skipmask;       // bit g: page g is not copied (block id 0 / out of range)
@@ -108,6 +108,11 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
   return v;
 }
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
@@ -129,15 +134,27 @@ __device__ __forceinline__ int64_t find_job(const JobDev* jobs, int64_t n, int64
   return lo;
 }
 
+// Factor entry {C[d0], C[d0+1], S[d0], S[d0+1]} stored as 4 x bf16 (low
+// half = d0): widening bf16 to fp32 is exact.
+__device__ __forceinline__ float4 widen_factors(uint2 w) {
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
+                     __uint_as_float(w.y & 0xffff0000u));
+}
+__device__ __forceinline__ float4 as_float4(uint4 w) {
+  return make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w));
+}
+
 // Rotates the K rows of the unit's pages held in shared memory (in place).
 // Task t of the unit -> page g, row, pair c; the factors come from the
 // unit's factor block staged beside the pages (fac_staged) or straight from
 // the factor buffer in global memory (L2 resident, shared by the heads).
-template <class E, bool NEOX, bool SCORE>
+// FC: factor entries are 4 x bf16 (8 bytes) instead of 4 x fp32 (16 bytes).
+template <class E, bool NEOX, bool SCORE, bool FC>
 __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* stage, int page_data,
-                                                 const StageMeta& st, const float4* fac_unit, bool fac_staged,
+                                                 const StageMeta& st, const uint8_t* fac_unit, bool fac_staged,
                                                  int64_t len, float* tok_dev, int tid, int nthreads) {
-  constexpr int U = 2;
+  constexpr int ES = FC ? 8 : 16;  // bytes per factor entry
+  constexpr int U = E::kPerVec > 8 ? 1 : 2;  // fp8: 16 elements a vector, one task in flight
   const int per_page = L.nrows * L.pair_vecs;
   const int ntask = per_page * st.npg;
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
@@ -166,19 +183,22 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
           slot[u] = (int)tok;
           lo[u] = lds128(base + off[u]);
           if (NEOX) hi[u] = lds128(base + off[u] + hi_off);
-          const float4* fq = fac_unit + tok * per_tok + c;
+          const uint8_t* fq = fac_unit + ((int)tok * per_tok + c) * ES;
           constexpr int NG = NEOX ? E::kPerVec / 2 : E::kPerVec / 4;
           if (fac_staged) {
             const uint32_t fa = smem_addr(fq);
 #pragma unroll
             for (int k = 0; k < NG; ++k) {
-              const uint4 w = lds128(fa + (uint32_t)(k * L.pair_vecs) * 16u);
-              q[u][k] = make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z),
-                                    __uint_as_float(w.w));
+              const uint32_t a = fa + (uint32_t)(k * L.pair_vecs * ES);
+              q[u][k] = FC ? widen_factors(lds64(a)) : as_float4(lds128(a));
             }
           } else {
 #pragma unroll
-            for (int k = 0; k < NG; ++k) q[u][k] = __ldg(fq + k * L.pair_vecs);
+            for (int k = 0; k < NG; ++k) {
+              const uint8_t* gp = fq + k * L.pair_vecs * ES;
+              q[u][k] = FC ? widen_factors(__ldg(reinterpret_cast<const uint2*>(gp)))
+                           : __ldg(reinterpret_cast<const float4*>(gp));
+            }
           }
         }
       }
@@ -205,7 +225,7 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
 // stage of the previous unit once its stores have read it.
 // Shared memory: [0,128) full/empty barriers | [128,kBulkHeader) stage meta |
 // per-stage deviation slots | stages (page g of a unit at g * page_data).
-template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE>
+template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE, bool FC>
 __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch p, BulkGeom g) {
   using E = Elem<KVT>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -290,9 +310,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
           mine.skipmask |= skip << q;
         }
         if (ROTATE && g.fac_off > 0 && jd.meta >= 0 && L.has_rot && p.metas[jd.meta].rotate) {
-          const int per_tok = L.half_rot / 2;
-          mine.fac = p.fac + (jd.fac_tok + (int64_t)pl0 * L.page_size) * per_tok;
-          mine.fac_bytes = (int32_t)((size_t)npg * page_factor_bytes(L.page_size, L.half_rot));
+          const int64_t tb = (int64_t)token_factor_bytes(L.half_rot, FC);
+          mine.fac = reinterpret_cast<const uint8_t*>(p.fac) + (jd.fac_tok + (int64_t)pl0 * L.page_size) * tb;
+          mine.fac_bytes = (int32_t)((size_t)npg * page_factor_bytes(L.page_size, L.half_rot, FC));
         }
         if (SCORE && jd.score_row >= 0 && jd.meta >= 0) {
           const MetaDev m = p.metas[jd.meta];
@@ -422,11 +442,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
         if (m.rotate) {
           uint8_t* stage = stages + (size_t)s * g.stage_bytes;
           const bool staged = g.fac_off > 0;
-          const float4* fac_unit =
-              staged ? reinterpret_cast<const float4*>(stage + g.fac_off)
-                     : p.fac + (j.fac_tok + (int64_t)st.pl0 * L.page_size) * (L.half_rot / 2);
-          rotate_unit_smem<E, NEOX, SCORE>(L, stage, g.page_data, st, fac_unit, staged, m.len,
-                                           devs + s * dev_stride, tid, kConsumers);
+          const uint8_t* fac_unit =
+              staged ? stage + g.fac_off
+                     : reinterpret_cast<const uint8_t*>(p.fac) +
+                           (j.fac_tok + (int64_t)st.pl0 * L.page_size) * (int64_t)token_factor_bytes(L.half_rot, FC);
+          rotate_unit_smem<E, NEOX, SCORE, FC>(L, stage, g.page_data, st, fac_unit, staged, m.len,
+                                               devs + s * dev_stride, tid, kConsumers);
           fence_proxy_async();
         }
       }
@@ -457,25 +478,30 @@ void launch_bulk(K kernel, const PageLaunch& p, const BulkGeom& g, int sm_count,
   DARIC_CUDA(cudaGetLastError());
 }
 
-template <int KVT>
+template <int KVT, bool FC>
 void bulk_rotate(const PageLaunch& p, const BulkGeom& g, bool neox, int sm, cudaStream_t s) {
   const bool sc = p.scores != nullptr;
   if (neox) {
-    if (sc) launch_bulk(bulk_pages_kernel<KVT, true, true, false, true>, p, g, sm, s);
-    else launch_bulk(bulk_pages_kernel<KVT, true, true, false, false>, p, g, sm, s);
+    if (sc) launch_bulk(bulk_pages_kernel<KVT, true, true, false, true, FC>, p, g, sm, s);
+    else launch_bulk(bulk_pages_kernel<KVT, true, true, false, false, FC>, p, g, sm, s);
   } else {
-    if (sc) launch_bulk(bulk_pages_kernel<KVT, false, true, false, true>, p, g, sm, s);
-    else launch_bulk(bulk_pages_kernel<KVT, false, true, false, false>, p, g, sm, s);
+    if (sc) launch_bulk(bulk_pages_kernel<KVT, false, true, false, true, FC>, p, g, sm, s);
+    else launch_bulk(bulk_pages_kernel<KVT, false, true, false, false, FC>, p, g, sm, s);
   }
+}
+template <int KVT>
+void bulk_rotate(const PageLaunch& p, const BulkGeom& g, bool neox, int sm, cudaStream_t s) {
+  if (g.fac_compact) bulk_rotate<KVT, true>(p, g, neox, sm, s);
+  else bulk_rotate<KVT, false>(p, g, neox, sm, s);
 }
 
 }  // namespace
 
 void launch_bulk_plain(const PageLaunch& p, const BulkGeom& g, bool gather, int sm, cudaStream_t s) {
   if (gather)
-    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, true, false, true, false>, p, g, sm, s);
+    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, true, false, true, false, false>, p, g, sm, s);
   else
-    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, true, false, false, false>, p, g, sm, s);
+    launch_bulk(bulk_pages_kernel<DARIC_DTYPE_BF16, true, false, false, false, false>, p, g, sm, s);
 }
 
 void launch_bulk_rotate(const PageLaunch& p, const BulkGeom& g, RotKey k, int sm, cudaStream_t s) {

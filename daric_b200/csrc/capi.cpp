@@ -440,47 +440,59 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // staged with the pages when three such stages still fit, else the consumer
 // warps read it from L2. DARIC_BULK_UNIT_PAGES / DARIC_BULK_FACTORS=l2 are
 // diagnostic overrides for A/B measurements.
-BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores) {
+BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores,
+                   int tab_dtype) {
   BulkGeom g{};
+  const char* fmt = std::getenv("DARIC_BULK_FACTOR_FORMAT");
+  const bool compact = rotate && tab_dtype == DARIC_DTYPE_BF16 && !(fmt && std::strcmp(fmt, "f32") == 0);
   size_t page = 0, slots = 0, fac = 0;
+  bool stageable = true;  // factor blocks are whole 16-byte words (bulk copy rule)
   for (const auto& l : layers) {
     page = std::max(page, (size_t)l.prefix_size * (size_t)l.suffix);
     slots = std::max(slots, (size_t)std::max(l.page_size, 1));
-    if (rotate) fac = std::max(fac, page_factor_bytes(l.page_size, l.half_rot));
+    if (rotate && l.has_rot) {
+      fac = std::max(fac, page_factor_bytes(l.page_size, l.half_rot, compact));
+      stageable = stageable && token_factor_bytes(l.half_rot, compact) % 16 == 0;
+    }
   }
   if (page == 0 || page >= (1u << 20)) return g;
-  size_t per_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / page));
+  const size_t max_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / page));
+  size_t pin = 0;
   if (const char* v = std::getenv("DARIC_BULK_UNIT_PAGES")) {
     const long want = std::strtol(v, nullptr, 10);
-    if (want >= 1 && want <= 8) per_unit = (size_t)want;
+    if (want >= 1 && want <= 8) pin = (size_t)want;
   }
   const char* fv = std::getenv("DARIC_BULK_FACTORS");
-  const bool allow_staged = !(fv && std::strcmp(fv, "l2") == 0);
+  const bool allow_staged = fac > 0 && stageable && !(fv && std::strcmp(fv, "l2") == 0);
   auto stages_for = [&](size_t stage, size_t dev) -> size_t {
     for (size_t k = 8; k >= 3; --k)
       if (kBulkHeader + round_up(k * dev, 128) + k * stage <= (size_t)dc.smem_optin) return k;
     return 0;
   };
-  const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
-  const size_t data = round_up(per_unit * page, 128);
-  size_t stage = data, fac_off = 0, ns = 0;
-  if (fac > 0 && allow_staged) {
-    const size_t with = round_up(data + per_unit * fac, 128);
-    ns = stages_for(with, dev);
-    if (ns >= 3) {
-      stage = with;
-      fac_off = data;
-    }
-  }
-  if (fac_off == 0) ns = stages_for(stage, dev);
-  if (ns < 3) return g;
-  g.nstage = (int32_t)ns;
-  g.stage_bytes = (int32_t)stage;
-  g.pages_per_unit = (int32_t)per_unit;
-  g.page_data = (int32_t)page;
-  g.dev_bytes = (int32_t)round_up(ns * dev, 128);
-  g.fac_off = (int32_t)fac_off;
-  return g;
+  auto fill = [&](size_t per_unit, bool staged) -> bool {
+    const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
+    const size_t data = round_up(per_unit * page, 128);
+    const size_t stage = staged ? round_up(data + per_unit * fac, 128) : data;
+    const size_t ns = stages_for(stage, dev);
+    if (ns < 3) return false;
+    g.nstage = (int32_t)ns;
+    g.stage_bytes = (int32_t)stage;
+    g.pages_per_unit = (int32_t)per_unit;
+    g.page_data = (int32_t)page;
+    g.dev_bytes = (int32_t)round_up(ns * dev, 128);
+    g.fac_off = staged ? (int32_t)data : 0;
+    g.fac_compact = compact ? 1 : 0;
+    return true;
+  };
+  // Staged factor blocks beat larger units: the largest unit (up to ~64 KiB)
+  // whose stages hold the factors, else the largest unit reading them from L2.
+  const size_t hi = pin ? pin : max_unit, lo = pin ? pin : 1;
+  if (allow_staged)
+    for (size_t u = hi; u >= lo; --u)
+      if (fill(u, true)) return g;
+  for (size_t u = hi; u >= lo; --u)
+    if (fill(u, false)) return g;
+  return BulkGeom{};
 }
 
 // Elements of a 16-byte vector / factors per rotation task of a layer.
@@ -510,8 +522,10 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   // jobs are 16-byte aligned and a unit fits three stages, else SIMT (units
   // of one page).
   const BulkGeom bg =
-      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate, rotate && scores) : BulkGeom{};
+      (jp.vec16 && bulk_pipeline_enabled()) ? plan_bulk(dc, layers, rotate, rotate && scores, key.tab_dtype)
+                                            : BulkGeom{};
   const int64_t upp = bg.nstage >= 3 ? bg.pages_per_unit : 1;
+  const bool compact = bg.nstage >= 3 && bg.fac_compact;
   std::vector<JobDev> jobs;
   jobs.reserve(job_index.size());
   // Factor runs: one per (rotating chunk, rotary table), padded to whole pages.
@@ -566,12 +580,12 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
     units += (jp.n_sel[i] + upp - 1) / upp;
   }
   if (units == 0) return;
-  // token offsets and float4 item offsets of the runs
+  // token offsets and entry offsets of the runs
   // runs of different rotary_dim use different token strides: each run
   // starts at the first token of its own stride past the previous run
   int64_t items = 0, fac_bytes = 0;
   for (size_t r = 0; r < runs.size(); ++r) {
-    const int64_t tok_bytes = (int64_t)runs[r].half_rot * 8;
+    const int64_t tok_bytes = (int64_t)token_factor_bytes(runs[r].half_rot, compact);
     runs[r].out_tok = (fac_bytes + tok_bytes - 1) / tok_bytes;
     runs[r].item_begin = items;
     items += runs[r].len * (runs[r].half_rot / 2);
@@ -604,6 +618,7 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
     fl.out = fac;
     fl.mode = mode;
     fl.fpv = factors_per_task(key.kv_dtype, key.neox != 0);
+    fl.compact = compact ? 1 : 0;
     launch_factors(fl, key.tab_dtype, dc.sm_count, stream);
   }
   PageLaunch p{};

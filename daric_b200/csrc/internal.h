@@ -176,14 +176,22 @@ struct FacJobDev {
 struct FactorLaunch {
   const FacJobDev* jobs;
   int64_t num_jobs;
-  int64_t total_items;  // float4 count
-  float4* out;
+  int64_t total_items;  // entry count (4 factors per entry)
+  void* out;
   int32_t mode;
   int32_t fpv;          // factors per rotation task
+  int32_t compact;      // entries are 4 x bf16 (8 bytes) instead of 4 x fp32
+  int32_t pad;
 };
 
-// Factor-block bytes of one page: page_size tokens x half_rot float2.
-__host__ __device__ inline size_t page_factor_bytes(int page_size, int half_rot) { return (size_t)page_size * half_rot * 8; }
+// Factor bytes of one token (half_rot (cos, sin) pairs): fp32, or bf16 when
+// the table is bf16 (its factors are bf16 values, so the narrow form is exact).
+__host__ __device__ inline size_t token_factor_bytes(int half_rot, bool compact) {
+  return (size_t)half_rot * (compact ? 4 : 8);
+}
+__host__ __device__ inline size_t page_factor_bytes(int page_size, int half_rot, bool compact = false) {
+  return (size_t)page_size * token_factor_bytes(half_rot, compact);
+}
 
 struct SelSegDev {
   int64_t col_off, len, pos0, k, blk_off, out_off;
@@ -239,6 +247,8 @@ struct BulkGeom {
   int32_t page_data;
   int32_t dev_bytes;
   int32_t fac_off;    // >0: the unit's factor block is staged at this offset; 0: read from L2
+  int32_t fac_compact;  // factors stored as bf16 pairs (bf16 tables) instead of fp32
+  int32_t pad;
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).

@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(kThreads) plain_pages_kernel(PageLaunch p) {
 }
 
 // ------------------------------------------------------ factor pre-pass --
-// One thread per float4 of the factor buffer: job f covers tokens [0, len)
+// One thread per entry of the factor buffer (4 factors: fp32 float4, or
+// bf16 x 4 packed in a uint2 when p.compact): job f covers tokens [0, len)
 // of one chunk (or segment) for one rotary table.
 template <int TABT>
 __global__ void __launch_bounds__(256) factor_kernel(FactorLaunch p) {
@@ -124,7 +125,16 @@ __global__ void __launch_bounds__(256) factor_kernel(FactorLaunch p) {
     if (p.mode == DARIC_ROPE_FLEXIBLE) { a += t; b += t; }
     const float2 f0 = rope_factor<T>(jb.table, jb.table_row, jb.half_rot, p.mode, a, b, d0);
     const float2 f1 = rope_factor<T>(jb.table, jb.table_row, jb.half_rot, p.mode, a, b, d0 + 1);
-    p.out[(jb.out_tok + t) * per_tok + k] = make_float4(f0.x, f1.x, f0.y, f1.y);
+    const int64_t e = (jb.out_tok + t) * per_tok + k;
+    if (p.compact) {
+      // bf16 table: every factor is already a bf16 value (rounded in
+      // rope_factor), so its upper 16 bits are the exact bf16 encoding
+      const uint32_t cw = (__float_as_uint(f0.x) >> 16) | (__float_as_uint(f1.x) & 0xffff0000u);
+      const uint32_t sw = (__float_as_uint(f0.y) >> 16) | (__float_as_uint(f1.y) & 0xffff0000u);
+      static_cast<uint2*>(p.out)[e] = make_uint2(cw, sw);
+    } else {
+      static_cast<float4*>(p.out)[e] = make_float4(f0.x, f1.x, f0.y, f1.y);
+    }
   }
 }
 
@@ -365,6 +375,8 @@ void launch_plain_pages(const PageLaunch& p, bool gather, bool vec16, int sm, cu
 
 void launch_factors(const FactorLaunch& p, int tab_dtype, int sm, cudaStream_t s) {
   if (p.total_items <= 0) return;
+  if (p.compact && tab_dtype != DARIC_DTYPE_BF16)
+    throw Error(DARIC_ERR_INVALID, "bf16 factor entries need a bf16 rotary table");
   int64_t blocks = (p.total_items + 255) / 256;
   const int64_t cap = (int64_t)sm * 8;
   if (blocks > cap) blocks = cap;

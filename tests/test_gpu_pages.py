@@ -26,14 +26,25 @@ def _setup(layout, dt, nb=24, bs=16, H=2, D=128, nlayers=2, seed=0):
     return g, layers, topo, pf
 
 
-@pytest.fixture(params=["bulk", "simt"])
+# page-kernel variants: the bulk-copy pipeline as planned (bf16 tables:
+# factors stored as bf16, staged with the pages), with fp32 factors, with
+# factors read from L2 in 3-page units (ragged last units), and the SIMT
+# vector kernel
+_VARIANTS = {
+    "bulk": {},
+    "bulk-f32": {"DARIC_BULK_FACTOR_FORMAT": "f32"},
+    "bulk-l2-u3": {"DARIC_BULK_FACTORS": "l2", "DARIC_BULK_UNIT_PAGES": "3"},
+    "simt": {"DARIC_PAGE_KERNEL": "simt"},
+}
+
+
+@pytest.fixture(params=list(_VARIANTS))
 def page_kernel(request, monkeypatch):
-    """Runs a test with each page-kernel implementation (bulk-copy pipeline
-    and SIMT vector kernel)."""
-    if request.param == "simt":
-        monkeypatch.setenv("DARIC_PAGE_KERNEL", "simt")
-    else:
-        monkeypatch.delenv("DARIC_PAGE_KERNEL", raising=False)
+    """Runs a test with each page-kernel implementation."""
+    for k in ("DARIC_PAGE_KERNEL", "DARIC_BULK_FACTOR_FORMAT", "DARIC_BULK_FACTORS", "DARIC_BULK_UNIT_PAGES"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in _VARIANTS[request.param].items():
+        monkeypatch.setenv(k, v)
     return request.param
 
 
