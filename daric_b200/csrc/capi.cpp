@@ -72,7 +72,8 @@ struct RingSlot {
   uint8_t* host = nullptr;
   uint8_t* dev = nullptr;
   size_t cap = 0;
-  cudaEvent_t done = nullptr;
+  cudaEvent_t done = nullptr;  // the call that used the slot last has finished with it
+  cudaEvent_t sent = nullptr;  // the slot's upload has landed
   bool pending = false;
 };
 
@@ -92,6 +93,7 @@ struct DeviceCtx {
   int sm_count = 0;
   int smem_optin = 0;
   int* err_word = nullptr;
+  cudaStream_t up_stream = nullptr;  // descriptor uploads (non-blocking stream)
   std::mutex mu;
   unsigned next = 0;
   RingSlot slots[kRingSlots];
@@ -115,20 +117,27 @@ DeviceCtx& device_ctx(int device) {
   for (auto& s : c->slots) {
     // all slots up front, so the first calls after start-up allocate nothing
     DARIC_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+    DARIC_CUDA(cudaEventCreateWithFlags(&s.sent, cudaEventDisableTiming));
     DARIC_CUDA(cudaHostAlloc((void**)&s.host, kSlotBytes, cudaHostAllocDefault));
     DARIC_CUDA(cudaMalloc((void**)&s.dev, kSlotBytes));
     s.cap = kSlotBytes;
   }
   DARIC_CUDA(cudaEventCreateWithFlags(&c->scratch.last, cudaEventDisableTiming));
+  DARIC_CUDA(cudaStreamCreateWithFlags(&c->up_stream, cudaStreamNonBlocking));
   auto& ref = *c;
   g_ctx[device] = std::move(c);
   return ref;
 }
 
 // One descriptor upload: a ring slot held for the duration of the call.
+// The host waits until the slot's previous call has finished with it, so the
+// copy can go out on the device's upload stream right away and overlap the
+// kernels still running on the caller's stream; the caller's stream waits
+// for it with an event. Under stream capture the copy is captured on the
+// caller's stream instead.
 class Upload {
  public:
-  Upload(DeviceCtx& c, size_t bytes) {
+  Upload(DeviceCtx& c, size_t bytes) : up_stream_(c.up_stream) {
     {
       std::lock_guard<std::mutex> g(c.mu);
       slot_ = &c.slots[c.next++ % kRingSlots];
@@ -154,14 +163,32 @@ class Upload {
   uint8_t* host() { return slot_->host; }
   uint8_t* dev() { return slot_->dev; }
   void send(size_t bytes, cudaStream_t s) {
-    if (bytes) DARIC_CUDA(cudaMemcpyAsync(slot_->dev, slot_->host, bytes, cudaMemcpyHostToDevice, s));
+    if (!bytes) return;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    DARIC_CUDA(cudaStreamIsCapturing(s, &cap));
+    if (cap != cudaStreamCaptureStatusNone) {
+      DARIC_CUDA(cudaMemcpyAsync(slot_->dev, slot_->host, bytes, cudaMemcpyHostToDevice, s));
+      return;
+    }
+    DARIC_CUDA(cudaMemcpyAsync(slot_->dev, slot_->host, bytes, cudaMemcpyHostToDevice, up_stream_));
+    DARIC_CUDA(cudaEventRecord(slot_->sent, up_stream_));
+    side_sent_ = true;
+    DARIC_CUDA(cudaStreamWaitEvent(s, slot_->sent, 0));
   }
   void finish(cudaStream_t s) {
     DARIC_CUDA(cudaEventRecord(slot_->done, s));
     slot_->pending = true;
+    finished_ = true;
+  }
+  // A call that failed after its upload went out: the slot's next user
+  // waits for that copy before it rewrites the pinned buffer.
+  ~Upload() {
+    if (side_sent_ && !finished_ && cudaEventRecord(slot_->done, up_stream_) == cudaSuccess) slot_->pending = true;
   }
 
  private:
+  cudaStream_t up_stream_;
+  bool side_sent_ = false, finished_ = false;
   RingSlot* slot_ = nullptr;
   std::unique_lock<std::mutex> lock_;
 };
@@ -1093,6 +1120,7 @@ int daric_score_select(const float* scores, int64_t num_layers, int64_t score_ld
     DARIC_CHECK(block_size > 0, "block_size must be positive");
     DARIC_CHECK(block_table != nullptr || block_table_numel == 0, "block_table is NULL");
     std::vector<SelSegDev> segs(num_segs);
+    int64_t max_len = 0;
     for (int64_t s = 0; s < num_segs; ++s) {
       SelSegDev& d = segs[s];
       d.col_off = seg_col_off[s];
@@ -1108,6 +1136,7 @@ int daric_score_select(const float* scores, int64_t num_layers, int64_t score_ld
       DARIC_CHECK(d.pos0 + d.len <= INT32_MAX, "positions exceed int32");
       const int64_t cap = mode == DARIC_SELECT_TOPK ? std::min(d.k, d.len) : d.len;
       DARIC_CHECK(d.out_off + cap <= out_ld, "segment " + std::to_string(s) + " output exceeds out_ld");
+      max_len = std::max(max_len, d.len);
     }
     DeviceCtx& dc = device_ctx(device);
     DeviceGuard dg(device);
@@ -1130,7 +1159,7 @@ int daric_score_select(const float* scores, int64_t num_layers, int64_t score_ld
     p.out_count = out_count;
     p.out_ld = out_ld;
     p.err = dc.err_word;
-    launch_score_select(p, (cudaStream_t)stream);
+    launch_score_select(p, max_len, dc.sm_count, (cudaStream_t)stream);
     up.finish((cudaStream_t)stream);
   });
 }

@@ -211,6 +211,8 @@ struct SelectLaunch {
   int32_t* out_count;
   int64_t out_ld;
   int* err;
+  int32_t cluster;    // CTAs per (segment, layer), a thread-block cluster
+  int32_t smem_keys;  // keys of a slice staged in shared memory (capacity)
 };
 
 struct RangeDev {
@@ -270,7 +272,8 @@ void launch_rotate_scatter(const PageLaunch& p, RotKey key, int sm_count, cudaSt
 void launch_rotate_inplace(const InplaceLaunch& p, RotKey key, int sm_count, cudaStream_t s);
 void launch_bulk_plain(const PageLaunch& p, const BulkGeom& g, bool gather, int sm_count, cudaStream_t s);
 void launch_bulk_rotate(const PageLaunch& p, const BulkGeom& g, RotKey key, int sm_count, cudaStream_t s);
-void launch_score_select(const SelectLaunch& p, cudaStream_t s);
+// max_len: longest segment of the call (picks the cluster size).
+void launch_score_select(SelectLaunch p, int64_t max_len, int sm_count, cudaStream_t s);
 void launch_ranges_to_slots(const RangeLaunch& p, cudaStream_t s);
 
 int* device_error_word(int device);  // per-device error word (lazily created)

@@ -1,16 +1,24 @@
 // Recompute-selection kernels.
 //
-//  * select_kernel : per (segment, layer) CTA, radix select of the k highest
-//    fp32 scores (8-bit digits, four histogram passes over an order-preserving
-//    32-bit key held in shared memory; per-warp histograms merged per pass),
-//    then a stable compaction in token order (warp ballots + one block scan)
-//    that emits the recompute positions and their paged-KV slots. Threshold
-//    mode skips the radix passes. Ties at the k-th score go to the lower
-//    token index.
+//  * select_kernel : per (segment, layer) a thread-block cluster of C CTAs
+//    (C = 1..8, picked by the host so that short calls still fill the SMs);
+//    CTA r of the cluster owns the r-th contiguous slice of the segment's
+//    columns and stages its order-preserving 32-bit keys in shared memory.
+//    Radix select of the k highest fp32 scores: four 8-bit digit passes, each
+//    a per-warp histogram of the slice merged per CTA, then over the cluster
+//    through distributed shared memory; every CTA derives the same digit.
+//    One exchange of per-CTA counts (keys above the k-th key, keys equal to
+//    it) then orders a stable compaction in token order (warp ballots + block
+//    scans) that emits the recompute positions and their paged-KV slots.
+//    Threshold mode skips the radix passes. Ties at the k-th score go to the
+//    lower token index.
 //  * ranges_kernel : expands [start, end) ranges of the DARIC policy
 //    (daric/adaption/policy.py:45-103) into positions and slots, the slot
 //    formula of the recompute sub-requests (integration/vllm/worker.py:310-346):
 //    slot = block_ids[p // bs] * bs + p % bs.
+#include <cooperative_groups.h>
+
+#include <cstdlib>
 #include <mutex>
 #include <set>
 
@@ -18,9 +26,11 @@
 
 namespace daric {
 namespace {
+namespace cg = cooperative_groups;
 
-constexpr int kSelThreads = 512;
+constexpr int kSelThreads = 256;  // 4 CTAs per SM (64 registers a thread)
 constexpr int kSelWarps = kSelThreads / 32;
+constexpr int kMaxCluster = 8;
 
 // Order-preserving key: larger float -> larger key. Every NaN maps to the
 // largest key (NaN ranks above +inf, as torch.topk orders it).
@@ -56,41 +66,60 @@ __device__ __forceinline__ int block_scan(int v, int* total, int* sm) {
   return x - v + (warp > 0 ? sm[warp - 1] : 0);
 }
 
-// Rows of up to kSmemKeys keys are staged in shared memory (one read of the
-// scores); longer rows are re-read from global memory (L2) on every pass.
+// Slices of up to kSmemKeys keys are staged in shared memory (one read of
+// the scores); longer slices are re-read from global memory (L2) per pass.
 constexpr int kSmemKeys = 12288;
 
 __device__ __forceinline__ uint32_t key_at(const float* row, const uint32_t* skeys, bool staged, int64_t i) {
   return staged ? skeys[i] : score_key(row[i]);
 }
 
-__global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
+// Columns of a segment of n keys owned by each CTA of a cluster of C.
+__host__ __device__ inline int64_t select_slice(int64_t n, int C) { return ((n + C - 1) / C + 31) & ~(int64_t)31; }
+
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(kSelThreads, 4) select_kernel(SelectLaunch p) {
   __shared__ uint32_t whist[kSelWarps][256];  // per-warp digit histograms
-  __shared__ uint32_t hist[256];
+  __shared__ uint32_t lhist[2][256];          // this slice's histogram, by pass parity (read by the cluster)
+  __shared__ uint32_t ghist[256];             // the segment's histogram (sum over the cluster)
+  __shared__ long long s_cnt[2];              // this slice: keys above the k-th key, keys equal to it
   __shared__ int scan_sm[32];
-  __shared__ uint32_t s_digit, s_above;
+  __shared__ uint32_t s_digit, s_above, s_lab;
   extern __shared__ uint32_t skeys[];
 
-  const int64_t si = blockIdx.x, l = blockIdx.y;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = (int)cluster.num_blocks();
+  const int me = (int)cluster.block_rank();
+  const int64_t si = blockIdx.x / C, l = blockIdx.y;
   const SelSegDev sg = p.segs[si];
-  const float* row = p.scores + l * p.score_ld + sg.col_off;
-  const int64_t n = sg.len;
+  const int64_t n_all = sg.len;
+  const int64_t chunk = select_slice(n_all, C);
+  const int64_t s0 = min(n_all, (int64_t)me * chunk);
+  const int64_t n = min(n_all - s0, chunk);  // this CTA's slice [s0, s0 + n)
+  const float* row = p.scores + l * p.score_ld + sg.col_off + s0;
   int32_t* oidx = p.out_idx + l * p.out_ld + sg.out_off;
   int64_t* oslot = p.out_slot + l * p.out_ld + sg.out_off;
   const bool topk = p.mode == DARIC_SELECT_TOPK;
-  const bool staged = n <= kSmemKeys;
-  const int warp_id = threadIdx.x >> 5;
+  const bool staged = n <= p.smem_keys;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
+  // Every branch below that skips cluster barriers depends only on the
+  // segment (k, n_all, mode), so the CTAs of a cluster take it together.
   uint32_t thr = 0;     // k-th largest key (top-k)
   int64_t take_eq = 0;  // keys equal to thr that are taken, lowest index first
   bool take_all = false;
+  long long my_sel = 0, my_eq = 0;
   if (topk) {
-    const int64_t k = sg.k < n ? sg.k : n;
+    const int64_t k = sg.k < n_all ? sg.k : n_all;
     if (k <= 0) {
-      if (threadIdx.x == 0) p.out_count[l * p.num_segs + si] = 0;
+      if (me == 0 && threadIdx.x == 0) p.out_count[l * p.num_segs + si] = 0;
       return;
     }
-    take_all = (k == n);
+    take_all = (k == n_all);
     if (!take_all) {
       if (staged) {  // all loads of a batch in flight before any key is stored
         constexpr int kBatch = 8;
@@ -110,11 +139,12 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
       }
       uint32_t prefix = 0, mask = 0;
       int64_t rem = k;
-      const int lane = threadIdx.x & 31;
-      for (int shift = 24; shift >= 0; shift -= 8) {
+      uint32_t* wh = whist[warp];
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        uint32_t* lh = lhist[pass & 1];
         for (int b = threadIdx.x; b < kSelWarps * 256; b += blockDim.x) (&whist[0][0])[b] = 0;
         __syncthreads();
-        uint32_t* wh = whist[warp_id];
         for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
           const uint32_t key = key_at(row, skeys, staged, i);
           if ((key & mask) == prefix) atomicAdd(&wh[(key >> shift) & 255u], 1u);
@@ -124,14 +154,23 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
           uint32_t t = 0;
 #pragma unroll
           for (int w = 0; w < kSelWarps; ++w) t += whist[w][b];
-          hist[b] = t;
+          lh[b] = t;
+        }
+        // lhist[pass & 1] of every CTA is complete after this barrier; the
+        // buffer is rewritten two passes later, after the next barrier, which
+        // no CTA reaches before it finished reading this one.
+        cluster.sync();
+        for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+          uint32_t t = 0;
+          for (int r = 0; r < C; ++r) t += cluster.map_shared_rank(lh, r)[b];
+          ghist[b] = t;
         }
         __syncthreads();
-        if (threadIdx.x < 32) {
+        if (warp == 0) {
           // lane L owns digits [248-8L, 255-8L], scanned from the top.
           uint32_t cnt[8], sum = 0;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) { cnt[q] = hist[255 - 8 * lane - q]; sum += cnt[q]; }
+          for (int q = 0; q < 8; ++q) { cnt[q] = ghist[255 - 8 * lane - q]; sum += cnt[q]; }
           uint32_t incl = sum;
 #pragma unroll
           for (int o = 1; o < 32; o <<= 1) {
@@ -150,27 +189,66 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
               acc += cnt[q];
             }
           }
+          __syncwarp();
+          // this slice's keys in the digits above the chosen one
+          const uint32_t d = s_digit;
+          uint32_t la = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint32_t dd = 255 - 8 * lane - q;
+            if (dd > d) la += lh[dd];
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) la += __shfl_xor_sync(0xffffffffu, la, o);
+          if (lane == 0) s_lab = la;
         }
         __syncthreads();
         prefix |= s_digit << shift;
         mask |= 255u << shift;
         rem -= s_above;
+        my_sel += s_lab;
+        if (pass == 3) my_eq = lh[s_digit];
         __syncthreads();
       }
       thr = prefix;
       take_eq = rem;
+    } else {
+      my_sel = n;
     }
+  } else {
+    int c = 0;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) c += row[i] >= p.threshold;
+    int tot;
+    block_scan(c, &tot, scan_sm);
+    my_sel = tot;
   }
 
-  // Compaction in token order: warp w owns the 512 consecutive keys
-  // [c0 + 512w, c0 + 512(w+1)) of each pass, as 16 rounds of 32 (lane = key),
+  // Counts of the lower-ranked slices give this slice's first output and the
+  // rank of its first tied key. The arrive below follows this CTA's last
+  // read of a peer's shared memory; the wait at the end keeps this CTA's
+  // shared memory alive until every peer has read it.
+  if (threadIdx.x == 0) {
+    s_cnt[0] = my_sel;
+    s_cnt[1] = my_eq;
+  }
+  cluster.sync();
+  long long sel_before = 0, eq_before = 0;
+  for (int r = 0; r < me; ++r) {
+    const long long* pc = cluster.map_shared_rank(s_cnt, r);
+    sel_before += pc[0];
+    eq_before += pc[1];
+  }
+  cluster_arrive();
+
+  // Compaction in token order: warp w owns the 256 consecutive keys
+  // [c0 + 256w, c0 + 256(w+1)) of each span, as 8 rounds of 32 (lane = key),
   // so ballots give in-warp ranks and one block scan orders the warps.
   const bool use_keys = topk && !take_all;
-  const int lane = threadIdx.x & 31, warp = warp_id;
   const uint32_t lt_mask = (1u << lane) - 1u;
-  constexpr int R = 16;
+  constexpr int R = 8;
   const int64_t span = (int64_t)kSelWarps * 32 * R;
-  int64_t running = 0, eq_seen = 0;
+  int64_t running = sel_before + (use_keys ? min((int64_t)eq_before, take_eq) : 0);
+  int64_t eq_seen = eq_before;
   for (int64_t c0 = 0; c0 < n; c0 += span) {
     const int64_t wb = c0 + (int64_t)warp * 32 * R;
     uint32_t selm[R], eqm[R];
@@ -218,7 +296,7 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
       if ((selm[r] >> lane) & 1u) {
         const int64_t i = wb + r * 32 + lane;
         const int64_t at = o + __popc(selm[r] & lt_mask);
-        const int64_t pos = sg.pos0 + i;
+        const int64_t pos = sg.pos0 + s0 + i;
         const int64_t bt = sg.blk_off + pos / p.block_size;
         int64_t slot = -1;
         if (bt >= 0 && bt < p.block_table_numel) {
@@ -233,7 +311,8 @@ __global__ void __launch_bounds__(kSelThreads) select_kernel(SelectLaunch p) {
     }
     running += sel_tot;
   }
-  if (threadIdx.x == 0) p.out_count[l * p.num_segs + si] = (int32_t)running;
+  if (me == C - 1 && threadIdx.x == 0) p.out_count[l * p.num_segs + si] = (int32_t)running;
+  cluster_wait();
 }
 
 __global__ void ranges_kernel(RangeLaunch p) {
@@ -258,12 +337,48 @@ __global__ void ranges_kernel(RangeLaunch p) {
   }
 }
 
+// Cluster size of a call: grow C (up to 8) while a slice does not fit the
+// key stage, or while the call has fewer than two CTAs per SM and slices
+// stay at 2048 keys or more. DARIC_SELECT_CLUSTER pins it for measurements.
+int select_cluster(int64_t items, int64_t max_len, int sm_count) {
+  if (const char* v = std::getenv("DARIC_SELECT_CLUSTER")) {  // diagnostic override (1, 2, 4, 8)
+    const int want = std::atoi(v);
+    if ((want == 1 || want == 2 || want == 4 || want == 8) && select_slice(max_len, want) <= kSmemKeys * 8)
+      return want;
+  }
+  int C = 1;
+  while (C < kMaxCluster) {
+    const bool too_long = select_slice(max_len, C) > kSmemKeys;
+    const bool few = items * C < 2 * (int64_t)sm_count && select_slice(max_len, 2 * C) >= 2048;
+    if (!too_long && !few) break;
+    C *= 2;
+  }
+  return C;
+}
+
+// Launch with the cluster size in p.cluster; dynamic shared memory holds the
+// largest slice (at most kSmemKeys keys). Allocates nothing.
+cudaError_t launch_select_cluster(const SelectLaunch& p, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.num_segs * p.cluster), (unsigned)p.num_layers, 1);
+  cfg.blockDim = dim3(kSelThreads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)p.smem_keys * sizeof(uint32_t);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, select_kernel, p);
+}
+
 }  // namespace
 
-void launch_score_select(const SelectLaunch& p, cudaStream_t s) {
+void launch_score_select(SelectLaunch p, int64_t max_len, int sm_count, cudaStream_t s) {
   if (p.num_segs <= 0 || p.num_layers <= 0) return;
   DARIC_CHECK(p.num_layers <= 65535, "score_select: at most 65535 layers per call");
-  const dim3 grid((unsigned)p.num_segs, (unsigned)p.num_layers, 1);
   {
     static std::mutex mu;
     static std::set<int> done;  // devices whose function attribute is set
@@ -276,8 +391,9 @@ void launch_score_select(const SelectLaunch& p, cudaStream_t s) {
       done.insert(dev);
     }
   }
-  select_kernel<<<grid, kSelThreads, kSmemKeys * sizeof(uint32_t), s>>>(p);
-  DARIC_CUDA(cudaGetLastError());
+  p.cluster = select_cluster(p.num_segs * p.num_layers, max_len, sm_count);
+  p.smem_keys = (int32_t)std::min<int64_t>(kSmemKeys, select_slice(max_len, p.cluster));
+  DARIC_CUDA(launch_select_cluster(p, s));
 }
 
 void launch_ranges_to_slots(const RangeLaunch& p, cudaStream_t s) {
@@ -316,9 +432,10 @@ namespace {
 std::mutex g_noalloc_mu;                              // guards the host staging and set-up
 daric::SelSegDev g_noalloc_host[kNoallocMaxSegs];     // host staging of one call's descriptors
 unsigned char* g_noalloc_dev[kNoallocMaxDevices];     // device address of the array, per device
+int g_noalloc_sms[kNoallocMaxDevices];                // SM count, per device
 
 // Set-up, once per device, with that device current: the array's device
-// address and the kernel's dynamic shared-memory limit.
+// address, the SM count and the kernel's dynamic shared-memory limit.
 unsigned char* noalloc_scratch(int device) {
   if (g_noalloc_dev[device]) return g_noalloc_dev[device];
   void* ptr = nullptr;
@@ -329,6 +446,9 @@ unsigned char* noalloc_scratch(int device) {
                            daric::kSmemKeys * (int)sizeof(uint32_t));
   if (e != cudaSuccess)
     throw daric::Error(DARIC_ERR_CUDA, std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(e));
+  e = cudaDeviceGetAttribute(&g_noalloc_sms[device], cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess)
+    throw daric::Error(DARIC_ERR_CUDA, std::string("cudaDeviceGetAttribute failed: ") + cudaGetErrorString(e));
   g_noalloc_dev[device] = static_cast<unsigned char*>(ptr);
   return g_noalloc_dev[device];
 }
@@ -362,6 +482,7 @@ void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, i
   } restore{device, prev};
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   unsigned char* scratch = noalloc_scratch(device);
+  int64_t max_len = 0;
   for (int64_t s = 0; s < num_segs; ++s) {
     daric::SelSegDev& d = g_noalloc_host[s];
     d.col_off = seg_col_off[s];
@@ -376,6 +497,7 @@ void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, i
     DARIC_CHECK(d.pos0 + d.len <= INT32_MAX, "positions exceed int32");
     const int64_t cap = mode == DARIC_SELECT_TOPK ? (d.k < d.len ? d.k : d.len) : d.len;
     DARIC_CHECK(d.out_off + cap <= out_ld, "segment " + std::to_string(s) + " output exceeds out_ld");
+    if (d.len > max_len) max_len = d.len;
   }
   // Pageable source: the copy is staged by the driver before it returns, so
   // the host staging can be reused by the next call right away. The error
@@ -400,9 +522,10 @@ void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, i
   p.out_count = out_count;
   p.out_ld = out_ld;
   p.err = reinterpret_cast<int*>(scratch + kNoallocSegBytes);
-  const dim3 grid((unsigned)num_segs, (unsigned)num_layers, 1);
-  daric::select_kernel<<<grid, daric::kSelThreads, daric::kSmemKeys * sizeof(uint32_t), stream>>>(p);
-  e = cudaGetLastError();
+  p.cluster = daric::select_cluster(num_segs * num_layers, max_len, g_noalloc_sms[device]);
+  const int64_t slice = daric::select_slice(max_len, p.cluster);
+  p.smem_keys = (int32_t)(slice < daric::kSmemKeys ? slice : daric::kSmemKeys);
+  e = daric::launch_select_cluster(p, stream);
   if (e != cudaSuccess) throw Error(DARIC_ERR_CUDA, std::string("noalloc select launch: ") + cudaGetErrorString(e));
 }
 

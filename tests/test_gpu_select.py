@@ -24,8 +24,11 @@ def _scores(L, T, seed, ties=False):
     return x.float()
 
 
+# long rows are split over a cluster of up to 8 CTAs (8192: eight slices of
+# 1024; 32768: eight of 4096), so ties and the k-th key straddle slices
 @pytest.mark.parametrize("T,ratio,ties", [(512, 0.15, False), (8192, 0.15, False), (1000, 0.3, True),
-                                          (33, 0.5, True), (32768, 0.2, False)])
+                                          (33, 0.5, True), (32768, 0.2, False), (8192, 0.3, True),
+                                          (20000, 0.05, True)])
 def test_topk_matches_oracle(T, ratio, ties):
     L, bs = 4, 16
     sc = _scores(L, T, seed=T, ties=ties)
@@ -75,6 +78,34 @@ def test_ragged_segments_threshold_and_edge_cases():
             idx, slot = out.get(l, s)
             np.testing.assert_array_equal(idx.cpu().numpy(), exp)
             np.testing.assert_array_equal(slot.cpu().numpy(), S.slots(tables[s].numpy(), exp, bs))
+
+
+def test_ragged_long_segments_split_over_a_cluster():
+    """Segments of very different lengths in one call: the long ones set a
+    cluster size of 4, the short ones leave some CTAs with empty slices."""
+    bs = 16
+    lens = [8000, 0, 17, 3000, 5, 1100]
+    ks = [1200, 3, 17, 2999, 0, 1100]
+    T = sum(lens)
+    g = torch.Generator().manual_seed(5)
+    sc = torch.randint(0, 50, (3, T), generator=g).float()  # many ties
+    sc[2, 100:200] = float("nan")
+    pos0 = [0, 0, 16, 32, 3, 7]
+    tables = [torch.randint(1, 1000, ((p + n + bs - 1) // bs + 1,), generator=g).int() for p, n in zip(pos0, lens)]
+    blk_off = np.concatenate([[0], np.cumsum([len(t) for t in tables])[:-1]])
+    bt = torch.cat(tables)
+    col = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    kw = dict(seg_len=lens, seg_pos0=pos0, seg_blk_off=blk_off)
+    for sel in (dict(k=ks), dict(threshold=25.0)):
+        out = score_select(sc.cuda(), bt.cuda(), bs, **kw, **sel)
+        for l in range(3):
+            for s in range(len(lens)):
+                row = sc[l, col[s]:col[s] + lens[s]].numpy()
+                exp = (S.topk_positions(row, ks[s]) if "k" in sel else S.threshold_positions(row, 25.0)) + pos0[s]
+                idx, slot = out.get(l, s)
+                np.testing.assert_array_equal(idx.cpu().numpy(), exp)
+                np.testing.assert_array_equal(slot.cpu().numpy(), S.slots(tables[s].numpy(), exp, bs))
+    assert _lib.device_errors(0) == 0
 
 
 def test_ptrs_to_slots_matches_oracle_and_policy():
