@@ -338,6 +338,9 @@ def run_ours(args):
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
+    warm_err = _lib.device_errors(local)
+    if warm_err:
+        raise RuntimeError(f"device error bits {warm_err} during warm-up; not timing a failing path")
     barrier()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]

@@ -127,7 +127,8 @@ def names_array(names) -> C.Array:
 
 
 def device_errors(device: int) -> int:
-    """Reads and clears the device error bits (1 block id, 2 table position, 4 block table)."""
+    """Reads and clears the device error bits (1 block id, 2 table position, 4 block table,
+    8 a bounded wait in the bulk pipeline timed out)."""
     v = C.c_int(0)
     check(load().daric_device_errors(int(device), C.byref(v)))
     return v.value

@@ -10,7 +10,7 @@
 // V bytes never pass through registers. Same byte mapping, block-0 skip,
 // rotation math and deviation scores as the SIMT kernels in page_kernels.cu.
 //
-// Every wait is bounded: an mbarrier wait that exceeds kWaitLimit rounds
+// Every wait is bounded: an mbarrier wait that exceeds kWaitNs (200 ms)
 // sets DEV_ERR_TIMEOUT, drains the copies this CTA has in flight (again with
 // a bound) and returns.
 #include <map>
@@ -23,21 +23,26 @@ namespace daric {
 namespace {
 using namespace dev;
 
+// Consumer warps per SM; a CTA has kConsumerWarps / ctas_per_sm of them plus
+// one producer warp (ctas_per_sm = 1, 2 or 4 CTAs share an SM).
 constexpr int kConsumerWarps = 16;
-constexpr int kBulkThreads = kConsumerWarps * 32 + 32;  // + one producer warp
+constexpr int kBulkThreads = kConsumerWarps * 32 + 32;  // largest CTA
 constexpr int kMaxStages = 8;
-constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // a bounded wait gives up after 200 ms
 
 constexpr int kMaxPagesPerUnit = 8;
 
-struct StageMeta {  // what the producer recorded when it issued a stage's loads
-  int64_t job;
+struct StageMeta {  // written by the producer lane that prefetched the unit
   uint8_t* base;          // layer data
+  const uint8_t* fac;     // the unit's factor block in the factor buffer (global)
+  float* sout;            // score output of the unit's first token (SCORE)
   int64_t stg_off;        // job's store offset
   int64_t page_stride;
   int64_t prefix_stride;
-  float* sout;            // score output of the unit's first token (SCORE)
-  const uint8_t* fac;     // factor block to stage with the pages (nullptr: none)
+  int64_t len;            // tokens of the chunk to rotate (rotating units)
+  int64_t fkey;           // factor block (group, page range); -1: none
+  int32_t layer;          // index into the launch's layer table
+  int32_t rot;            // the unit's K rows are rotated
   int32_t pl0;            // first page (job-local) of the unit
   int32_t npg;            // pages in the unit
   int32_t skipmask;       // bit g: page g is not copied (block id 0 / out of range)
@@ -45,7 +50,9 @@ struct StageMeta {  // what the producer recorded when it issued a stage's loads
   int32_t rbytes;         // bytes per region
   int32_t n_sel;          // pages of the job
   int32_t sn;             // tokens with a score to write
-  int32_t fac_bytes;      // bytes of the staged factor block
+  int32_t fac_bytes;      // bytes of the factor block
+  int32_t fbuf;           // shared-memory factor buffer holding the block
+  int32_t pad;
   int32_t blk[kMaxPagesPerUnit];
 };
 static_assert(128 + kMaxStages * sizeof(StageMeta) <= kBulkHeader, "stage meta exceeds the header");
@@ -76,11 +83,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for the phase with the given parity: false after kWaitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t k = 0; k < kWaitLimit; ++k)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t k = 1;; ++k) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if ((k & 63) == 0 && global_ns() - t0 > kWaitNs) return false;
+  }
 }
 __device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -125,11 +140,11 @@ __device__ __forceinline__ void cta_range(int64_t total, int64_t& begin, int64_t
   end = begin + q + (b < r ? 1 : 0);
 }
 
-__device__ __forceinline__ int64_t find_job(const JobDev* jobs, int64_t n, int64_t unit) {
+__device__ __forceinline__ int64_t find_group(const GroupDev* groups, int64_t n, int64_t unit) {
   int64_t lo = 0, hi = n - 1;
   while (lo < hi) {
     const int64_t mid = (lo + hi + 1) >> 1;
-    if (__ldg(&jobs[mid].unit_begin) <= unit) lo = mid; else hi = mid - 1;
+    if (__ldg(&groups[mid].unit_begin) <= unit) lo = mid; else hi = mid - 1;
   }
   return lo;
 }
@@ -150,7 +165,7 @@ __device__ __forceinline__ float4 as_float4(uint4 w) {
 // the factor buffer in global memory (L2 resident, shared by the heads).
 // FC: factor entries are 4 x bf16 (8 bytes) instead of 4 x fp32 (16 bytes).
 template <class E, bool NEOX, bool SCORE, bool FC>
-__device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* stage, int page_data,
+__device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* stage, int pages_per_unit,
                                                  const StageMeta& st, const uint8_t* fac_unit, bool fac_staged,
                                                  int64_t len, float* tok_dev, int tid, int nthreads) {
   constexpr int ES = FC ? 8 : 16;  // bytes per factor entry
@@ -160,7 +175,8 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
   const int per_tok = L.half_rot / 2;
   const int64_t tok_base = (int64_t)st.pl0 * L.page_size;
-  const uint32_t base = smem_addr(stage) + (uint32_t)L.k_prefix * (uint32_t)st.rbytes;
+  // plane-major stage: region pf of page g at (pf * pages_per_unit + g) * rbytes
+  const uint32_t base = smem_addr(stage) + (uint32_t)(L.k_prefix * pages_per_unit) * (uint32_t)st.rbytes;
   // warp-uniform trip count (score_add shuffles across the warp)
   for (int b0 = tid; b0 - (tid & 31) < ntask; b0 += U * nthreads) {
     uint4 lo[U], hi[U];
@@ -179,7 +195,7 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
         const int sl = row_slot(L, row);
         const int64_t tok = (int64_t)g * L.page_size + sl;  // unit token
         if (!((st.skipmask >> g) & 1) && tok_base + tok < len) {
-          off[u] = g * page_data + row * L.row_bytes + c * 16;
+          off[u] = g * st.rbytes + row * L.row_bytes + c * 16;
           slot[u] = (int)tok;
           lo[u] = lds128(base + off[u]);
           if (NEOX) hi[u] = lds128(base + off[u] + hi_off);
@@ -217,14 +233,22 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
   }
 }
 
-// Warp-specialised pipeline. Warps 0..kConsumerWarps-1 rotate; the last
-// warp is the producer: its 32 lanes prefetch the copy plans of 32 units at
-// a time, and lane 0 issues the bulk loads of unit u into stage u % NS
-// (full[s] completes when the bytes land), waits until every consumer warp
-// has released the unit (empty[s]), issues the bulk stores, and reuses the
-// stage of the previous unit once its stores have read it.
+// Warp-specialised pipeline. Warps 0..cwarps-1 rotate (in CG groups that
+// take alternate units); the last warp is the producer. Its 32 lanes prefetch the copy plans of 32 units at a time; for
+// unit u the lane that prefetched it writes the stage metadata and arms
+// full[u % NS], then the warp issues the unit's bulk loads (one region per
+// lane). When every consumer warp has released the unit (empty[s]) the warp
+// issues its bulk stores (one region per lane) and reuses the stage of the
+// previous unit once those stores have read it.
+// Units run page range by page range across the jobs of a group, so
+// consecutive units share a factor block: the producer loads a block into
+// one of two factor buffers only when the key changes (its bytes complete on
+// the unit's full barrier; later units see it through their own, later,
+// full waits), after the units that read that buffer's previous block have
+// been released.
 // Shared memory: [0,128) full/empty barriers | [128,kBulkHeader) stage meta |
-// per-stage deviation slots | stages (page g of a unit at g * page_data).
+// per-stage deviation slots | two factor buffers | stages, plane-major
+// (region pf of page g at (pf * pages_per_unit + g) * rbytes).
 template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE, bool FC>
 __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch p, BulkGeom g) {
   using E = Elem<KVT>;
@@ -233,33 +257,35 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   uint64_t* empty = full + kMaxStages;
   StageMeta* meta = reinterpret_cast<StageMeta*>(smem + 128);
   float* devs = reinterpret_cast<float*>(smem + kBulkHeader);  // NS x dev_stride floats
-  uint8_t* stages = smem + kBulkHeader + g.dev_bytes;
+  uint8_t* fbufs = smem + kBulkHeader + g.dev_bytes;
+  uint8_t* stages = fbufs + (g.fac_off ? 2 * g.fac_buf : 0);
   const int NS = g.nstage;
-  const int G = g.pages_per_unit;
+  const int PU = g.pages_per_unit;
   const int dev_stride = g.dev_bytes / (4 * NS);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const bool producer = warp == kConsumerWarps;
-  constexpr int kConsumers = kConsumerWarps * 32;
+  const int cwarps = (int)(blockDim.x >> 5) - 1;  // consumer warps of this CTA
+  const bool producer = warp == cwarps;
+  // consumer groups: group c rotates units c, c + CG, c + 2 CG, ... so CG
+  // units are in the consumers' hands at once. NS is a multiple of CG, so a
+  // stage is always rotated by the same group, which waits for its phases in
+  // order (a parity wait must never run two phases ahead).
+  const int CG = (g.cgroups > 1 && g.nstage % g.cgroups == 0) ? g.cgroups : 1;
+  const int gwarps = cwarps / CG;
 
   int64_t ubeg, uend;
   cta_range(p.total_units, ubeg, uend);
   if (ubeg >= uend) return;
   const int64_t n = uend - ubeg;
 
-  // address of region pf of job-local page pl (block blk) on the source /
-  // destination side
-  auto store_region = [&](const StageMeta& st, int pl, int pf) -> uint8_t* {
-    return p.store_mut + st.stg_off + ((int64_t)pf * st.n_sel + pl) * st.rbytes;
-  };
-  auto layer_region = [&](const StageMeta& st, int32_t blk, int pf) -> uint8_t* {
-    return st.base + (int64_t)pf * st.prefix_stride + (int64_t)blk * st.page_stride;
-  };
+  // Region pf of job-local page pl (block blk): store side at
+  // stg_off + (pf * n_sel + pl) * rbytes, layer side at
+  // base + pf * prefix_stride + blk * page_stride.
 
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], gwarps);
     }
     mbar_init_fence();
   }
@@ -269,30 +295,35 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
 
   if (producer) {
     const unsigned FULL = 0xffffffffu;
-    int64_t jc = find_job(p.jobs, p.num_jobs, ubeg);
+    int64_t gcur = find_group(p.groups, p.num_groups, ubeg);
     int64_t batch = -1;
-    // this lane's unit of the current batch
-    StageMeta mine{};
+    StageMeta mine{};  // this lane's unit of the current batch
     auto prefetch = [&](int64_t b) {  // all lanes
       const int64_t i = b * 32 + lane;
-      int64_t j = jc;
+      int64_t gi = gcur;
       mine.npg = 0;
       mine.skipmask = 0;
       mine.sn = 0;
+      mine.rot = 0;
       mine.fac = nullptr;
       mine.fac_bytes = 0;
+      mine.fkey = -1;
+      mine.len = 0;
       if (i < n) {
         const int64_t u = ubeg + i;
-        while (j + 1 < p.num_jobs && p.jobs[j + 1].unit_begin <= u) ++j;
-        const JobDev jd = p.jobs[j];
+        while (gi + 1 < p.num_groups && p.groups[gi + 1].unit_begin <= u) ++gi;
+        const GroupDev G = p.groups[gi];
+        const int64_t local = u - G.unit_begin;
+        const int r = (int)(local / G.cnt);
+        const JobDev jd = p.jobs[G.j0 + (local - (int64_t)r * G.cnt)];
         const LayerDev& L = p.layers[jd.layer];
-        const int pl0 = (int)(u - jd.unit_begin) * G;
-        const int npg = min(G, jd.n_sel - pl0);
-        mine.job = j;
+        const int pl0 = r * PU;
+        const int npg = min(PU, jd.n_sel - pl0);
         mine.base = L.base;
         mine.stg_off = jd.stg_off;
         mine.page_stride = L.page_stride;
         mine.prefix_stride = L.prefix_stride;
+        mine.layer = jd.layer;
         mine.pl0 = pl0;
         mine.npg = npg;
         mine.nreg = L.prefix_size;
@@ -309,98 +340,173 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
           mine.blk[q] = blk;
           mine.skipmask |= skip << q;
         }
-        if (ROTATE && g.fac_off > 0 && jd.meta >= 0 && L.has_rot && p.metas[jd.meta].rotate) {
-          const int64_t tb = (int64_t)token_factor_bytes(L.half_rot, FC);
-          mine.fac = reinterpret_cast<const uint8_t*>(p.fac) + (jd.fac_tok + (int64_t)pl0 * L.page_size) * tb;
-          mine.fac_bytes = (int32_t)((size_t)npg * page_factor_bytes(L.page_size, L.half_rot, FC));
-        }
-        if (SCORE && jd.score_row >= 0 && jd.meta >= 0) {
+        if (ROTATE && jd.meta >= 0) {
           const MetaDev m = p.metas[jd.meta];
-          const int64_t tok0 = (int64_t)pl0 * L.page_size;
-          const int64_t left = m.len - tok0;
-          const int64_t cap = (int64_t)npg * L.page_size;
-          mine.sn = (int32_t)(left < 0 ? 0 : (left < cap ? left : cap));
-          mine.sout = p.scores + (int64_t)jd.score_row * p.score_ld + m.score_col + tok0;
+          if (L.has_rot && m.rotate) {
+            const int64_t tb = (int64_t)token_factor_bytes(L.half_rot, FC);
+            mine.rot = 1;
+            mine.len = m.len;
+            mine.fac = reinterpret_cast<const uint8_t*>(p.fac) + (jd.fac_tok + (int64_t)pl0 * L.page_size) * tb;
+            mine.fac_bytes = (int32_t)((size_t)npg * page_factor_bytes(L.page_size, L.half_rot, FC));
+            mine.fkey = (gi << 24) | r;
+          }
+          if (SCORE && jd.score_row >= 0) {
+            const int64_t tok0 = (int64_t)pl0 * L.page_size;
+            const int64_t left = m.len - tok0;
+            const int64_t cap = (int64_t)npg * L.page_size;
+            mine.sn = (int32_t)(left < 0 ? 0 : (left < cap ? left : cap));
+            mine.sout = p.scores + (int64_t)jd.score_row * p.score_ld + m.score_col + tok0;
+          }
         }
       }
-      jc = __shfl_sync(FULL, j, 31);
+      gcur = __shfl_sync(FULL, gi, 31);
     };
-    auto shfl64 = [&](auto v, int k) {
-      return (decltype(v))__shfl_sync(FULL, (unsigned long long)v, k);
-    };
-    // loads of unit i into stage i % NS (warp-synchronous: every lane calls)
-    auto issue = [&](int64_t i) {
+    // factor buffers: the block each holds and the last unit that reads it
+    // (scalar pairs: no local-memory arrays)
+    long long fkey0 = -1, fkey1 = -1;
+    int64_t last0 = -1, last1 = -1;
+    int cur = 1;
+    int64_t waited = -1;  // empty[] of every unit <= waited has completed
+    // loads of unit i into stage i % NS (warp-synchronous: every lane calls);
+    // false when a wait timed out
+    auto issue = [&](int64_t i) -> bool {
       const int64_t b = i / 32;
       if (b != batch) {
         prefetch(b);
         batch = b;
       }
       const int k = (int)(i - b * 32);
-      StageMeta st;
-      st.job = __shfl_sync(FULL, mine.job, k);
-      st.base = shfl64(mine.base, k);
-      st.stg_off = __shfl_sync(FULL, mine.stg_off, k);
-      st.page_stride = __shfl_sync(FULL, mine.page_stride, k);
-      st.prefix_stride = __shfl_sync(FULL, mine.prefix_stride, k);
-      st.sout = shfl64(mine.sout, k);
-      st.pl0 = __shfl_sync(FULL, mine.pl0, k);
-      st.npg = __shfl_sync(FULL, mine.npg, k);
-      st.skipmask = __shfl_sync(FULL, mine.skipmask, k);
-      st.nreg = __shfl_sync(FULL, mine.nreg, k);
-      st.rbytes = __shfl_sync(FULL, mine.rbytes, k);
-      st.n_sel = __shfl_sync(FULL, mine.n_sel, k);
-      st.sn = __shfl_sync(FULL, mine.sn, k);
-      st.fac = shfl64(mine.fac, k);
-      st.fac_bytes = __shfl_sync(FULL, mine.fac_bytes, k);
-#pragma unroll
-      for (int q = 0; q < kMaxPagesPerUnit; ++q) st.blk[q] = __shfl_sync(FULL, mine.blk[q], k);
-      if (lane != 0) return;
       const int s = (int)(i % NS);
-      meta[s] = st;
-      const int live = st.npg - __popc(st.skipmask);
-      if (live == 0) {
-        mbar_arrive(&full[s]);
-        return;
-      }
-      uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-      const uint32_t fb = (uint32_t)st.fac_bytes;
-      mbar_arrive_expect_tx(&full[s], (uint32_t)(live * st.nreg * st.rbytes) + fb);
-      if (fb) bulk_load(buf + g.fac_off, st.fac, fb, &full[s]);
-      for (int q = 0; q < st.npg; ++q) {
-        if ((st.skipmask >> q) & 1) continue;
-        for (int pf = 0; pf < st.nreg; ++pf) {
-          const uint8_t* src = GATHER ? layer_region(st, st.blk[q], pf) : store_region(st, st.pl0 + q, pf);
-          bulk_load(buf + (size_t)q * g.page_data + (size_t)pf * st.rbytes, src, (uint32_t)st.rbytes, &full[s]);
+      const long long fkey = __shfl_sync(FULL, (long long)mine.fkey, k);
+      const int npg = __shfl_sync(FULL, mine.npg, k);
+      const int live = npg - __popc(__shfl_sync(FULL, mine.skipmask, k));
+      int fbuf = 0;
+      uint32_t fload = 0;
+      if (g.fac_off && fkey >= 0 && live > 0) {
+        if (fkey == (cur ? fkey1 : fkey0)) {
+          fbuf = cur;
+        } else {
+          const int f = cur ^ 1;
+          const int64_t x = f ? last1 : last0;
+          // units up to x may still read the buffer's old block: wait for
+          // each of them (consumer groups release units out of order)
+          for (int64_t y = waited + 1; y <= x; ++y) {
+            const bool ok = mbar_wait(&empty[y % NS], (uint32_t)((y / NS) & 1));
+            if (__any_sync(FULL, !ok)) return false;
+          }
+          if (f) fkey1 = fkey; else fkey0 = fkey;
+          cur = f;
+          fbuf = f;
+          fload = (uint32_t)__shfl_sync(FULL, mine.fac_bytes, k);
         }
+        if (fbuf) last1 = i; else last0 = i;
       }
+      if (lane == k) {
+        mine.fbuf = fbuf;
+        meta[s] = mine;
+        // the arrival (with the byte count) precedes every copy; scatter
+        // loads whole planes (skipped pages included), gather live regions
+        const int pages = GATHER ? live : mine.npg;
+        if (live == 0) mbar_arrive(&full[s]);
+        else mbar_arrive_expect_tx(&full[s], (uint32_t)(pages * mine.nreg * mine.rbytes) + fload);
+      }
+      if (live == 0) return true;
+      __syncwarp();
+      // operands from the stage metadata (shared memory), read once before
+      // the copies (which clobber memory)
+      const StageMeta& sm = meta[s];
+      const int nreg = sm.nreg, rbytes = sm.rbytes, pl0 = sm.pl0, skipm = sm.skipmask, nsel = sm.n_sel;
+      const int npgs = sm.npg;
+      // scatter: the unit's pages of a plane are contiguous in the store, one
+      // copy per plane; gather: one copy per live region
+      const int nops = GATHER ? npgs * nreg : nreg;
+      uint8_t* const lbase = sm.base;
+      const int64_t stg_off = sm.stg_off, pstride = sm.page_stride, fstride = sm.prefix_stride;
+      const uint8_t* const fsrc = sm.fac;
+      uint8_t* buf = stages + (size_t)s * g.stage_bytes;
+      for (int o = lane; o < nops + (fload ? 1 : 0); o += 32) {
+        uint8_t* dst;
+        const uint8_t* src;
+        uint32_t bytes;
+        if (o == nops) {
+          dst = fbufs + (size_t)fbuf * g.fac_buf;
+          src = fsrc;
+          bytes = fload;
+        } else if (!GATHER) {
+          dst = buf + (size_t)o * PU * rbytes;
+          src = p.store + stg_off + ((int64_t)o * nsel + pl0) * rbytes;
+          bytes = (uint32_t)(npgs * rbytes);
+        } else {
+          const int q = o / nreg, pf = o - q * nreg;
+          if ((skipm >> q) & 1) continue;
+          dst = buf + ((size_t)pf * PU + q) * rbytes;
+          src = lbase + (int64_t)pf * fstride + (int64_t)sm.blk[q] * pstride;
+          bytes = (uint32_t)rbytes;
+        }
+        bulk_load(dst, src, bytes, &full[s]);
+      }
+      return true;
     };
-    int64_t issued = 0;
-    for (; issued < NS - 1 && issued < n; ++issued) issue(issued);
-    bool prev_stored = false;  // unit i-1 has a pending store group (lane 0)
-    int64_t i = 0;
-    for (; i < n; ++i) {
-      const int s = (int)(i % NS);
-      const bool ok = mbar_wait(&empty[s], (uint32_t)((i / NS) & 1));
-      if (__any_sync(FULL, !ok)) {
-        if (lane == 0) atomicOr(p.err, DEV_ERR_TIMEOUT);
+    bool ok = true;
+    int64_t issued = 0;  // units whose loads are armed
+    while (issued < NS - 1 && issued < n) {
+      if (!issue(issued)) {
+        ok = false;
         break;
       }
-      const StageMeta& st = meta[s];
-      const bool stored = st.npg > __popc(st.skipmask);
-      if (lane == 0 && stored) {
+      ++issued;
+    }
+    bool prev_stored = false;  // unit i-1 has a pending store group (every lane)
+    int64_t i = 0;
+    for (; ok && i < n; ++i) {
+      const int s = (int)(i % NS);
+      const bool got = mbar_wait(&empty[s], (uint32_t)((i / NS) & 1));
+      if (__any_sync(FULL, !got)) {
+        ok = false;
+        break;
+      }
+      waited = i;
+      // operands from the stage metadata, read once before the copies
+      const StageMeta& sm = meta[s];
+      const int nreg = sm.nreg, rbytes = sm.rbytes, pl0 = sm.pl0, skipm = sm.skipmask, nsel = sm.n_sel;
+      const int nops = sm.npg * nreg;
+      uint8_t* const lbase = sm.base;
+      const int64_t stg_off = sm.stg_off, pstride = sm.page_stride, fstride = sm.prefix_stride;
+      const int sn = sm.sn;
+      float* const sout = sm.sout;
+      const bool stored = sm.npg > __popc(skipm);
+      if (stored) {
+        // stores spread over the lanes; every lane commits a bulk group per
+        // stored unit (empty for lanes without a region), so the groups of
+        // all lanes stay in step for the waits below
         uint8_t* buf = stages + (size_t)s * g.stage_bytes;
-        for (int q = 0; q < st.npg; ++q) {
-          if ((st.skipmask >> q) & 1) continue;
-          for (int pf = 0; pf < st.nreg; ++pf) {
-            uint8_t* dst = GATHER ? store_region(st, st.pl0 + q, pf) : layer_region(st, st.blk[q], pf);
-            bulk_store(dst, buf + (size_t)q * g.page_data + (size_t)pf * st.rbytes, (uint32_t)st.rbytes);
+        // gather without skipped pages: one store per plane (contiguous in
+        // the store); else one per live region
+        const bool whole = GATHER && skipm == 0;
+        const int sops = whole ? nreg : nops;
+        for (int o = lane; o < sops; o += 32) {
+          uint8_t* dst;
+          const uint8_t* src;
+          uint32_t bytes;
+          if (whole) {
+            dst = p.store_mut + stg_off + ((int64_t)o * nsel + pl0) * rbytes;
+            src = buf + (size_t)o * PU * rbytes;
+            bytes = (uint32_t)(sm.npg * rbytes);
+          } else {
+            const int q = o / nreg, pf = o - q * nreg;
+            if ((skipm >> q) & 1) continue;
+            dst = GATHER ? p.store_mut + stg_off + ((int64_t)pf * nsel + pl0 + q) * rbytes
+                         : lbase + (int64_t)pf * fstride + (int64_t)sm.blk[q] * pstride;
+            src = buf + ((size_t)pf * PU + q) * rbytes;
+            bytes = (uint32_t)rbytes;
           }
+          bulk_store(dst, src, bytes);
         }
         bulk_commit();
       }
       if (SCORE) {
         float* dv = devs + s * dev_stride;
-        for (int q = lane; q < st.sn; q += 32) st.sout[q] = dv[q];
+        for (int q = lane; q < sn; q += 32) sout[q] = dv[q];
         __syncwarp();
         for (int q = lane; q < dev_stride; q += 32) dv[q] = 0.f;
       }
@@ -408,49 +514,44 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       // the next load goes into the stage of unit i-1: its stores must have
       // read it (unit i's group, committed last, may still be pending)
       if (issued < n) {
-        if (lane == 0 && prev_stored) {
+        if (prev_stored) {
           if (stored) bulk_wait_read<1>(); else bulk_wait_read<0>();
         }
         __syncwarp();
-        issue(issued);
-        ++issued;
+        if (issue(issued)) ++issued;
+        else ok = false;
       }
       prev_stored = stored;
       __syncwarp();
     }
-    if (i < n && lane == 0) {
-      // timed out: drain the loads still in flight into this CTA's stages
-      for (int64_t k = i + 1; k < issued; ++k) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
+    if (!ok && lane == 0) {
+      atomicOr(p.err, DEV_ERR_TIMEOUT);
+      // drain the loads that may still be in flight into this CTA's stages
+      // (units not yet released by the consumers)
+      for (int64_t k = i; k < issued; ++k) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
     }
-    if (lane == 0) bulk_wait_all();
+    bulk_wait_all();
     return;
   }
 
   // consumers
-  for (int64_t i = 0; i < n; ++i) {
+  const int grp = warp / gwarps;
+  const int gtid = tid - grp * gwarps * 32;
+  for (int64_t i = grp; i < n; i += CG) {
     const int s = (int)(i % NS);
     if (!mbar_wait(&full[s], (uint32_t)((i / NS) & 1))) {
       atomicOr(p.err, DEV_ERR_TIMEOUT);
       break;
     }
     const StageMeta& st = meta[s];
-    if (ROTATE && st.npg > __popc(st.skipmask)) {
-      const JobDev j = p.jobs[st.job];
-      const LayerDev& L = p.layers[j.layer];
-      if (j.meta >= 0 && L.has_rot) {
-        const MetaDev m = p.metas[j.meta];
-        if (m.rotate) {
-          uint8_t* stage = stages + (size_t)s * g.stage_bytes;
-          const bool staged = g.fac_off > 0;
-          const uint8_t* fac_unit =
-              staged ? stage + g.fac_off
-                     : reinterpret_cast<const uint8_t*>(p.fac) +
-                           (j.fac_tok + (int64_t)st.pl0 * L.page_size) * (int64_t)token_factor_bytes(L.half_rot, FC);
-          rotate_unit_smem<E, NEOX, SCORE, FC>(L, stage, g.page_data, st, fac_unit, staged, m.len,
-                                               devs + s * dev_stride, tid, kConsumers);
-          fence_proxy_async();
-        }
-      }
+    if (ROTATE && st.rot && st.npg > __popc(st.skipmask)) {
+      const LayerDev& L = p.layers[st.layer];
+      uint8_t* stage = stages + (size_t)s * g.stage_bytes;
+      const bool staged = g.fac_off > 0;
+      const uint8_t* fac_unit = staged ? fbufs + (size_t)st.fbuf * g.fac_buf : st.fac;
+      rotate_unit_smem<E, NEOX, SCORE, FC>(L, stage, PU, st, fac_unit, staged, st.len,
+                                           devs + s * dev_stride, gtid, gwarps * 32);
+      fence_proxy_async();
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -473,8 +574,10 @@ void launch_bulk(K kernel, const PageLaunch& p, const BulkGeom& g, int sm_count,
       cur = smem;
     }
   }
-  const int grid = (int)(p.total_units < sm_count ? p.total_units : sm_count);
-  kernel<<<grid, kBulkThreads, smem, s>>>(p, g);
+  const int64_t ctas = (int64_t)sm_count * g.ctas_per_sm;
+  const int grid = (int)(p.total_units < ctas ? p.total_units : ctas);
+  const int threads = (kConsumerWarps / g.ctas_per_sm + 1) * 32;
+  kernel<<<grid, threads, smem, s>>>(p, g);
   DARIC_CUDA(cudaGetLastError());
 }
 

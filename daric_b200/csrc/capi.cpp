@@ -91,7 +91,8 @@ struct Scratch {
 struct DeviceCtx {
   int device = -1;
   int sm_count = 0;
-  int smem_optin = 0;
+  int smem_optin = 0;  // per block
+  int smem_sm = 0;     // per SM
   int* err_word = nullptr;
   cudaStream_t up_stream = nullptr;  // descriptor uploads (non-blocking stream)
   std::mutex mu;
@@ -111,6 +112,7 @@ DeviceCtx& device_ctx(int device) {
   c->device = device;
   DARIC_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
   DARIC_CUDA(cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  DARIC_CUDA(cudaDeviceGetAttribute(&c->smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device));
   DeviceGuard dg(device);
   DARIC_CUDA(cudaMalloc(&c->err_word, sizeof(int)));
   DARIC_CUDA(cudaMemset(c->err_word, 0, sizeof(int)));
@@ -462,14 +464,19 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Bulk pipeline geometry for a launch, or nstage = 0 when the pipeline
 // cannot hold three stages (load, rotate and store in flight together).
-// Small pages are packed into units of up to 8 consecutive pages of a job so
-// that every unit carries about 64 KiB; the rotating units' factor block is
-// staged with the pages when three such stages still fit, else the consumer
-// warps read it from L2. DARIC_BULK_UNIT_PAGES / DARIC_BULK_FACTORS=l2 are
-// diagnostic overrides for A/B measurements.
+// A unit's producer work is about constant, so units carry up to about
+// 64 KiB: up to 8 consecutive pages of a job (the largest that fits three
+// stages). Units run page range by page range across the layers of a chunk,
+// so one factor block serves many consecutive units: it sits in one of two
+// shared-memory factor buffers when they fit too, else the consumer warps
+// read it from L2.
+// One CTA per SM unless DARIC_BULK_CTAS asks for 2 or 4 (each with its own
+// producer warp and a share of the consumer warps and shared memory);
+// DARIC_BULK_CGROUPS splits the consumer warps into 2 or 4 groups.
+// DARIC_BULK_CTAS, DARIC_BULK_UNIT_PAGES, DARIC_BULK_FACTORS=l2 and
+// DARIC_BULK_FACTOR_FORMAT=f32 pin choices for A/B measurements.
 BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores,
                    int tab_dtype) {
-  BulkGeom g{};
   const char* fmt = std::getenv("DARIC_BULK_FACTOR_FORMAT");
   const bool compact = rotate && tab_dtype == DARIC_DTYPE_BF16 && !(fmt && std::strcmp(fmt, "f32") == 0);
   size_t page = 0, slots = 0, fac = 0;
@@ -482,43 +489,58 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
       stageable = stageable && token_factor_bytes(l.half_rot, compact) % 16 == 0;
     }
   }
-  if (page == 0 || page >= (1u << 20)) return g;
-  const size_t max_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / page));
-  size_t pin = 0;
-  if (const char* v = std::getenv("DARIC_BULK_UNIT_PAGES")) {
-    const long want = std::strtol(v, nullptr, 10);
-    if (want >= 1 && want <= 8) pin = (size_t)want;
-  }
+  if (page == 0 || page >= (1u << 20)) return BulkGeom{};
+  auto env_int = [](const char* name, long lo, long hi) -> long {
+    const char* v = std::getenv(name);
+    if (!v) return 0;
+    const long x = std::strtol(v, nullptr, 10);
+    return x >= lo && x <= hi ? x : 0;
+  };
+  const size_t pin_unit = (size_t)env_int("DARIC_BULK_UNIT_PAGES", 1, 8);
+  const long pin_ctas = env_int("DARIC_BULK_CTAS", 1, 4);
+  const long pin_groups = env_int("DARIC_BULK_CGROUPS", 1, 4);
   const char* fv = std::getenv("DARIC_BULK_FACTORS");
   const bool allow_staged = fac > 0 && stageable && !(fv && std::strcmp(fv, "l2") == 0);
-  auto stages_for = [&](size_t stage, size_t dev) -> size_t {
-    for (size_t k = 8; k >= 3; --k)
-      if (kBulkHeader + round_up(k * dev, 128) + k * stage <= (size_t)dc.smem_optin) return k;
-    return 0;
-  };
-  auto fill = [&](size_t per_unit, bool staged) -> bool {
-    const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
-    const size_t data = round_up(per_unit * page, 128);
-    const size_t stage = staged ? round_up(data + per_unit * fac, 128) : data;
-    const size_t ns = stages_for(stage, dev);
-    if (ns < 3) return false;
-    g.nstage = (int32_t)ns;
-    g.stage_bytes = (int32_t)stage;
-    g.pages_per_unit = (int32_t)per_unit;
-    g.page_data = (int32_t)page;
-    g.dev_bytes = (int32_t)round_up(ns * dev, 128);
-    g.fac_off = staged ? (int32_t)data : 0;
-    g.fac_compact = compact ? 1 : 0;
-    return true;
-  };
-  // Staged factor blocks beat larger units: the largest unit (up to ~64 KiB)
-  // whose stages hold the factors, else the largest unit reading them from L2.
-  const size_t hi = pin ? pin : max_unit, lo = pin ? pin : 1;
-  if (allow_staged)
+  // CTAs per SM (one unless pinned)
+  int ctas = 1;
+  if (pin_ctas == 1 || pin_ctas == 2 || pin_ctas == 4) ctas = (int)pin_ctas;
+  for (; ctas >= 1; ctas /= 2) {
+    const size_t budget =
+        std::min<size_t>((size_t)dc.smem_optin, (size_t)dc.smem_sm / (size_t)ctas - 1024);  // 1 KiB reserved per CTA
+    const size_t groups = (pin_groups == 2 || pin_groups == 4) ? (size_t)pin_groups : 1;
+    // stage count: at least 3, a multiple of the consumer groups
+    auto stages_for = [&](size_t stage, size_t dev, size_t fixed) -> size_t {
+      for (size_t k = 8; k >= 3; --k)
+        if (k % groups == 0 && kBulkHeader + round_up(k * dev, 128) + fixed + k * stage <= budget) return k;
+      return 0;
+    };
+    BulkGeom g{};
+    auto fill = [&](size_t per_unit, bool staged) -> bool {
+      const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
+      const size_t stage = round_up(per_unit * page, 128);
+      const size_t fbuf = staged ? round_up(per_unit * fac, 128) : 0;
+      const size_t ns = stages_for(stage, dev, 2 * fbuf);
+      if (ns < 3) return false;
+      g.nstage = (int32_t)ns;
+      g.stage_bytes = (int32_t)stage;
+      g.pages_per_unit = (int32_t)per_unit;
+      g.page_data = (int32_t)page;
+      g.dev_bytes = (int32_t)round_up(ns * dev, 128);
+      g.fac_off = staged ? (int32_t)(kBulkHeader + g.dev_bytes) : 0;
+      g.fac_buf = (int32_t)fbuf;
+      g.fac_compact = compact ? 1 : 0;
+      g.ctas_per_sm = ctas;
+      g.cgroups = (int32_t)groups;
+      return true;
+    };
+    // The largest unit (up to the per-CTA target) that fits three stages,
+    // with its factors in two shared-memory factor buffers when those fit
+    // too, else read from L2.
+    const size_t max_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / ((size_t)ctas * page)));
+    const size_t hi = pin_unit ? pin_unit : max_unit, lo = pin_unit ? pin_unit : 1;
     for (size_t u = hi; u >= lo; --u)
-      if (fill(u, true)) return g;
-  for (size_t u = hi; u >= lo; --u)
-    if (fill(u, false)) return g;
+      if ((allow_staged && fill(u, true)) || fill(u, false)) return g;
+  }
   return BulkGeom{};
 }
 
@@ -622,17 +644,47 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
     if (j.meta >= 0 && metas[j.meta].rotate)
       j.fac_tok = runs[run_of[std::make_pair((int64_t)j.meta, (const void*)layers[j.layer].table)]].out_tok;
   runs.erase(std::remove_if(runs.begin(), runs.end(), [](const FacJobDev& f) { return f.len <= 0; }), runs.end());
+  // Bulk pipeline unit order: groups of consecutive jobs of one chunk with
+  // the same page count and factor run (same tokens, same factors).
+  std::vector<GroupDev> groups;
+  if (bg.nstage >= 3) {
+    int64_t u = 0;
+    for (size_t a = 0; a < jobs.size();) {
+      const JobDev& A = jobs[a];
+      const LayerDev& LA = layers[A.layer];
+      size_t e = a + 1;
+      for (; e < jobs.size(); ++e) {
+        const JobDev& B = jobs[e];
+        const LayerDev& LB = layers[B.layer];
+        if (B.meta != A.meta || B.n_sel != A.n_sel || B.fac_tok != A.fac_tok || LB.page_size != LA.page_size ||
+            LB.half_rot != LA.half_rot || LB.has_rot != LA.has_rot)
+          break;
+      }
+      GroupDev gd{};
+      gd.unit_begin = u;
+      gd.j0 = (int32_t)a;
+      gd.cnt = (int32_t)(e - a);
+      gd.n_sel = A.n_sel;
+      gd.nranges = (int32_t)((A.n_sel + upp - 1) / upp);
+      u += (int64_t)gd.nranges * gd.cnt;
+      groups.push_back(gd);
+      a = e;
+    }
+    DARIC_CHECK(u == units, "internal: bulk unit count mismatch");
+  }
   DeviceGuard dg(jp.device);
   Blob b;
   const size_t o_layers = b.add(layers.size() * sizeof(LayerDev));
   const size_t o_jobs = b.add(jobs.size() * sizeof(JobDev));
   const size_t o_metas = b.add(metas.size() * sizeof(MetaDev));
   const size_t o_runs = b.add(runs.size() * sizeof(FacJobDev));
+  const size_t o_groups = b.add(groups.size() * sizeof(GroupDev));
   Upload up(dc, b.size);
   std::memcpy(up.host() + o_layers, layers.data(), layers.size() * sizeof(LayerDev));
   std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
   if (!metas.empty()) std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
   if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
+  if (!groups.empty()) std::memcpy(up.host() + o_groups, groups.data(), groups.size() * sizeof(GroupDev));
   std::unique_ptr<ScratchLease> lease;
   if (fac_bytes > 0) lease = std::make_unique<ScratchLease>(dc, (size_t)fac_bytes, stream);
   float4* fac = lease ? reinterpret_cast<float4*>(lease->ptr()) : nullptr;
@@ -663,6 +715,8 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   p.score_ld = score_ld;
   p.err = dc.err_word;
   p.fac = fac;
+  p.groups = reinterpret_cast<const GroupDev*>(up.dev() + o_groups);
+  p.num_groups = (int64_t)groups.size();
   if (bg.nstage >= 3) {
     if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
     else launch_bulk_plain(p, bg, gather, dc.sm_count, stream);

@@ -133,6 +133,19 @@ struct PageLaunch {
   int64_t score_ld;
   int* err;                  // device error word
   const float4* fac;         // rotary factors (factor pre-pass output)
+  const struct GroupDev* groups;  // bulk pipeline unit order
+  int64_t num_groups;
+};
+
+// Bulk pipeline unit order: consecutive jobs of one chunk with the same page
+// count and factor run form a group; its units go page range by page range
+// and, within a range, job by job (unit = range r of job j0 + l at
+// unit_begin + r * cnt + l), so consecutive units share their factor block.
+struct GroupDev {
+  int64_t unit_begin;
+  int32_t j0, cnt;     // jobs [j0, j0 + cnt)
+  int32_t n_sel;       // pages of each job
+  int32_t nranges;     // ceil(n_sel / pages_per_unit)
 };
 
 // In-place rotation segments.
@@ -239,25 +252,31 @@ enum : int {
 };
 
 // Geometry of the bulk-copy pipeline: NSTAGE shared-memory stages of
-// stage_bytes each, after the header and a dev_bytes region of per-slot
-// deviations. A unit is up to pages_per_unit consecutive pages of one job;
-// page g of a unit occupies [g * page_data, (g + 1) * page_data) of its stage.
+// stage_bytes each, after the header, a dev_bytes region of per-slot
+// deviations and the factor buffers. A unit is up to pages_per_unit
+// consecutive pages of one job, plane-major in its stage: region pf of page g
+// at (pf * pages_per_unit + g) * rbytes. page_data = largest page of the
+// launch (prefix_size x region bytes).
 struct BulkGeom {
   int32_t nstage;
   int32_t stage_bytes;
   int32_t pages_per_unit;
   int32_t page_data;
   int32_t dev_bytes;
-  int32_t fac_off;    // >0: the unit's factor block is staged at this offset; 0: read from L2
+  int32_t fac_off;      // >0: offset of the two factor buffers (one unit's factors each); 0: read from L2
+  int32_t fac_buf;      // bytes of one factor buffer
   int32_t fac_compact;  // factors stored as bf16 pairs (bf16 tables) instead of fp32
-  int32_t pad;
+  int32_t ctas_per_sm;  // 1, 2 or 4 CTAs (each with its own producer warp) per SM
+  int32_t cgroups;      // consumer-warp groups (1, 2 or 4) taking alternate units
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
 constexpr int kBulkHeader = 2048;
 
+// [header | deviation slots | factor buffers | stages]
 inline size_t bulk_smem_bytes(const BulkGeom& g) {
-  return kBulkHeader + (size_t)g.dev_bytes + (size_t)g.nstage * g.stage_bytes;
+  return kBulkHeader + (size_t)g.dev_bytes + (g.fac_off ? 2 * (size_t)g.fac_buf : 0) +
+         (size_t)g.nstage * g.stage_bytes;
 }
 
 // ------------------------------------------------------------ launchers --
