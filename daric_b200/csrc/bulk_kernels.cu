@@ -241,13 +241,13 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
 // issues its bulk stores (one region per lane) and reuses the stage of the
 // previous unit once those stores have read it.
 // Units run page range by page range across the jobs of a group, so
-// consecutive units share a factor block: the producer loads a block into
-// one of two factor buffers only when the key changes (its bytes complete on
-// the unit's full barrier; later units see it through their own, later,
-// full waits), after the units that read that buffer's previous block have
-// been released.
+// consecutive units share a factor block: the producer loads a block into a
+// factor buffer (the other one of two, or the only one) only when the key
+// changes (its bytes complete on the unit's full barrier; later units see it
+// through their own, later, full waits), after the units that read that
+// buffer's previous block have been released.
 // Shared memory: [0,128) full/empty barriers | [128,kBulkHeader) stage meta |
-// per-stage deviation slots | two factor buffers | stages, plane-major
+// per-stage deviation slots | factor buffers | stages, plane-major
 // (region pf of page g at (pf * pages_per_unit + g) * rbytes).
 template <int KVT, bool NEOX, bool ROTATE, bool GATHER, bool SCORE, bool FC>
 __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch p, BulkGeom g) {
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   StageMeta* meta = reinterpret_cast<StageMeta*>(smem + 128);
   float* devs = reinterpret_cast<float*>(smem + kBulkHeader);  // NS x dev_stride floats
   uint8_t* fbufs = smem + kBulkHeader + g.dev_bytes;
-  uint8_t* stages = fbufs + (g.fac_off ? 2 * g.fac_buf : 0);
+  uint8_t* stages = fbufs + (g.fac_off ? g.fac_nbuf * g.fac_buf : 0);
   const int NS = g.nstage;
   const int PU = g.pages_per_unit;
   const int dev_stride = g.dev_bytes / (4 * NS);
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
         if (fkey == (cur ? fkey1 : fkey0)) {
           fbuf = cur;
         } else {
-          const int f = cur ^ 1;
+          const int f = g.fac_nbuf == 2 ? cur ^ 1 : 0;
           const int64_t x = f ? last1 : last0;
           // units up to x may still read the buffer's old block: wait for
           // each of them (consumer groups release units out of order)

@@ -468,13 +468,16 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // 64 KiB: up to 8 consecutive pages of a job (the largest that fits three
 // stages). Units run page range by page range across the layers of a chunk,
 // so one factor block serves many consecutive units: it sits in one of two
-// shared-memory factor buffers when they fit too, else the consumer warps
+// shared-memory factor buffers when they fit too (else in one, loaded once
+// the units reading the previous block are done), else the consumer warps
 // read it from L2.
-// One CTA per SM unless DARIC_BULK_CTAS asks for 2 or 4 (each with its own
-// producer warp and a share of the consumer warps and shared memory);
+// Pages of 8 KiB or less run two CTAs per SM, others one (DARIC_BULK_CTAS
+// pins 1, 2 or 4; each CTA has its own producer warp and a share of the
+// consumer warps and shared memory);
 // DARIC_BULK_CGROUPS splits the consumer warps into 2 or 4 groups.
-// DARIC_BULK_CTAS, DARIC_BULK_UNIT_PAGES, DARIC_BULK_FACTORS=l2 and
-// DARIC_BULK_FACTOR_FORMAT=f32 pin choices for A/B measurements.
+// DARIC_BULK_CTAS, DARIC_BULK_UNIT_PAGES, DARIC_BULK_FACTORS=l2,
+// DARIC_BULK_FACTOR_BUFFERS and DARIC_BULK_FACTOR_FORMAT=f32 pin choices for
+// A/B measurements.
 BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores,
                    int tab_dtype) {
   const char* fmt = std::getenv("DARIC_BULK_FACTOR_FORMAT");
@@ -501,8 +504,9 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
   const long pin_groups = env_int("DARIC_BULK_CGROUPS", 1, 4);
   const char* fv = std::getenv("DARIC_BULK_FACTORS");
   const bool allow_staged = fac > 0 && stageable && !(fv && std::strcmp(fv, "l2") == 0);
-  // CTAs per SM (one unless pinned)
-  int ctas = 1;
+  // CTAs per SM: pages of 8 KiB or less (one KV head of 128 at block 16)
+  // run two CTAs per SM, so two producers feed the SM's copy engine
+  int ctas = page <= 8 * 1024 ? 2 : 1;
   if (pin_ctas == 1 || pin_ctas == 2 || pin_ctas == 4) ctas = (int)pin_ctas;
   for (; ctas >= 1; ctas /= 2) {
     const size_t budget =
@@ -515,19 +519,20 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
       return 0;
     };
     BulkGeom g{};
-    auto fill = [&](size_t per_unit, bool staged) -> bool {
+    auto fill = [&](size_t per_unit, int nbuf) -> bool {  // nbuf factor buffers (0: L2)
       const size_t dev = scores ? round_up(per_unit * slots * 4, 16) : 0;
       const size_t stage = round_up(per_unit * page, 128);
-      const size_t fbuf = staged ? round_up(per_unit * fac, 128) : 0;
-      const size_t ns = stages_for(stage, dev, 2 * fbuf);
+      const size_t fbuf = nbuf ? round_up(per_unit * fac, 128) : 0;
+      const size_t ns = stages_for(stage, dev, (size_t)nbuf * fbuf);
       if (ns < 3) return false;
       g.nstage = (int32_t)ns;
       g.stage_bytes = (int32_t)stage;
       g.pages_per_unit = (int32_t)per_unit;
       g.page_data = (int32_t)page;
       g.dev_bytes = (int32_t)round_up(ns * dev, 128);
-      g.fac_off = staged ? (int32_t)(kBulkHeader + g.dev_bytes) : 0;
+      g.fac_off = nbuf ? (int32_t)(kBulkHeader + g.dev_bytes) : 0;
       g.fac_buf = (int32_t)fbuf;
+      g.fac_nbuf = nbuf;
       g.fac_compact = compact ? 1 : 0;
       g.ctas_per_sm = ctas;
       g.cgroups = (int32_t)groups;
@@ -535,11 +540,15 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
     };
     // The largest unit (up to the per-CTA target) that fits three stages,
     // with its factors in two shared-memory factor buffers when those fit
-    // too, else read from L2.
+    // too, else in one, else read from L2.
     const size_t max_unit = std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / ((size_t)ctas * page)));
     const size_t hi = pin_unit ? pin_unit : max_unit, lo = pin_unit ? pin_unit : 1;
-    for (size_t u = hi; u >= lo; --u)
-      if ((allow_staged && fill(u, true)) || fill(u, false)) return g;
+    const long pin_nbuf = env_int("DARIC_BULK_FACTOR_BUFFERS", 1, 2);
+    for (size_t u = hi; u >= lo; --u) {
+      if (allow_staged && pin_nbuf != 1 && fill(u, 2)) return g;
+      if (allow_staged && pin_nbuf != 2 && fill(u, 1)) return g;
+      if (fill(u, 0)) return g;
+    }
   }
   return BulkGeom{};
 }

@@ -226,20 +226,28 @@ __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, 
   }
 }
 
-// Adds each lane's deviation `v` to dev[slot] (slot < 0: nothing). When the
-// whole warp works on one slot (a warp's tasks are usually heads of one
-// token) the warp sums first and one lane adds; otherwise every lane adds.
-// Must be called by all 32 lanes of the warp.
+// Adds a per-task deviation to its token's slot. The lanes of a warp that
+// share a slot form aligned groups (a warp's tasks are consecutive: pair
+// tasks of a row, then the rows (heads) of a token); the warp finds the
+// largest such group size, sums within the groups by shuffles and one lane
+// per group adds. Must be called by all 32 lanes of the warp.
 __device__ __forceinline__ void score_add(float* dev, int slot, float v) {
   const unsigned full = 0xffffffffu;
   const int s0 = __shfl_sync(full, slot, 0);
-  if (__all_sync(full, slot == s0)) {
+  if (__all_sync(full, slot == s0)) {  // the whole warp on one token
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(full, v, o);
     if ((threadIdx.x & 31) == 0 && s0 >= 0) atomicAdd(&dev[s0], v);
-  } else if (slot >= 0) {
-    atomicAdd(&dev[slot], v);
+    return;
   }
+  int seg = 1;
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) {
+    if (!__all_sync(full, __shfl_xor_sync(full, slot, o) == slot)) break;
+    v += __shfl_xor_sync(full, v, o);
+    seg = o << 1;
+  }
+  if (((threadIdx.x & 31) & (seg - 1)) == 0 && slot >= 0) atomicAdd(&dev[slot], v);
 }
 
 // Token slot of K row `row` of a page region.

@@ -263,11 +263,13 @@ struct BulkGeom {
   int32_t pages_per_unit;
   int32_t page_data;
   int32_t dev_bytes;
-  int32_t fac_off;      // >0: offset of the two factor buffers (one unit's factors each); 0: read from L2
+  int32_t fac_off;      // >0: offset of the factor buffers (one unit's factors each); 0: read from L2
   int32_t fac_buf;      // bytes of one factor buffer
+  int32_t fac_nbuf;     // factor buffers: 2 (load the next block while the last is read) or 1
   int32_t fac_compact;  // factors stored as bf16 pairs (bf16 tables) instead of fp32
   int32_t ctas_per_sm;  // 1, 2 or 4 CTAs (each with its own producer warp) per SM
   int32_t cgroups;      // consumer-warp groups (1, 2 or 4) taking alternate units
+  int32_t pad;
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
@@ -275,7 +277,7 @@ constexpr int kBulkHeader = 2048;
 
 // [header | deviation slots | factor buffers | stages]
 inline size_t bulk_smem_bytes(const BulkGeom& g) {
-  return kBulkHeader + (size_t)g.dev_bytes + (g.fac_off ? 2 * (size_t)g.fac_buf : 0) +
+  return kBulkHeader + (size_t)g.dev_bytes + (g.fac_off ? (size_t)g.fac_nbuf * g.fac_buf : 0) +
          (size_t)g.nstage * g.stage_bytes;
 }
 

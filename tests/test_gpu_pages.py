@@ -29,8 +29,8 @@ def _setup(layout, dt, nb=24, bs=16, H=2, D=128, nlayers=2, seed=0):
 # page-kernel variants: the bulk-copy pipeline as planned (bf16 tables:
 # factors stored as bf16, staged with the pages; small pages: 4 CTAs per
 # SM), with fp32 factors, with factors read from L2 in 3-page units (ragged
-# last units), with 1 and 2 CTAs per SM, with 4 consumer-warp groups, and
-# the SIMT vector kernel
+# last units), with 1 and 2 CTAs per SM, with 4 consumer-warp groups, with
+# one factor buffer, and the SIMT vector kernel
 _VARIANTS = {
     "bulk": {},
     "bulk-f32": {"DARIC_BULK_FACTOR_FORMAT": "f32"},
@@ -38,6 +38,7 @@ _VARIANTS = {
     "bulk-1cta": {"DARIC_BULK_CTAS": "1"},
     "bulk-2cta": {"DARIC_BULK_CTAS": "2"},
     "bulk-4groups": {"DARIC_BULK_CGROUPS": "4"},
+    "bulk-1facbuf": {"DARIC_BULK_FACTOR_BUFFERS": "1"},
     "simt": {"DARIC_PAGE_KERNEL": "simt"},
 }
 
@@ -46,7 +47,7 @@ _VARIANTS = {
 def page_kernel(request, monkeypatch):
     """Runs a test with each page-kernel implementation."""
     for k in ("DARIC_PAGE_KERNEL", "DARIC_BULK_FACTOR_FORMAT", "DARIC_BULK_FACTORS", "DARIC_BULK_UNIT_PAGES",
-              "DARIC_BULK_CTAS", "DARIC_BULK_CGROUPS"):
+              "DARIC_BULK_CTAS", "DARIC_BULK_CGROUPS", "DARIC_BULK_FACTOR_BUFFERS"):
         monkeypatch.delenv(k, raising=False)
     for k, v in _VARIANTS[request.param].items():
         monkeypatch.setenv(k, v)
