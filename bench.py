@@ -72,6 +72,13 @@ CONFIGS = {
     # deviation scores all-reduced before a top-20% selection
     4: dict(name="llama3-70b-32k-tp", layers=80, kv_heads=8, head_dim=128, block_size=16, theta=5e5,
             ratio=0.20, requests=1, chunks=64, chunk_len=(512, 512), suffix=0, scores="deviation", tp=True),
+    # Mistral-7B shape, requests of U[2048, 16384] tokens in 512-token chunks of
+    # which a hit-ratio share is reused (loaded), the rest uncached; one step = a batch of 16
+    # requests per rank (the 512-request job runs as 512 / (16 N) steps per rank);
+    # --hit and --recompute sweep the two ratios
+    5: dict(name="mistral-7b-dp-sweep", layers=32, kv_heads=8, head_dim=128, block_size=16, theta=1e6,
+            ratio=0.15, requests=16, req_len=(2048, 16384), chunk=512, hit=0.75, suffix=0,
+            scores="lognormal", tp=False),
 }
 
 
@@ -93,17 +100,27 @@ class Workload:
             h0, h1 = tp_head_range(rank, world, H)
             H = h1 - h0
         self.heads = H
-        # chunk lengths per request, placement and shuffled saved positions
-        lo, hi = c["chunk_len"]
+        # reused chunks per request: (length, start in the request); placement and
+        # shuffled saved positions
         reqs = []
         for r in range(c["requests"]):
-            lens = [lo] * c["chunks"] if lo == hi else \
-                [int(x) * bs for x in torch.randint(lo // bs, hi // bs + 1, (c["chunks"],), generator=g)]
-            reqs.append(lens)
+            if "req_len" in c:  # request of U[a, b] tokens, chunked; a hit-ratio share is reused
+                a, b = c["req_len"]
+                n = int(torch.randint(a // bs, b // bs + 1, (1,), generator=g)) * bs
+                full = [min(c["chunk"], n - s0) for s0 in range(0, n, c["chunk"])]
+                at = np.concatenate([[0], np.cumsum(full)[:-1]]).tolist()
+                hit = (torch.rand(len(full), generator=g) < c["hit"]).tolist()
+                reqs.append([(ln, st) for ln, st, h in zip(full, at, hit) if h])
+            else:
+                lo, hi = c["chunk_len"]
+                lens = [lo] * c["chunks"] if lo == hi else \
+                    [int(x) * bs for x in torch.randint(lo // bs, hi // bs + 1, (c["chunks"],), generator=g)]
+                reqs.append(list(zip(lens, np.concatenate([[0], np.cumsum(lens)[:-1]]).tolist())))
         self.chunk_len, self.new_pos, self.old_pos, self.req_of = [], [], [], []
         self.req_tokens = []
-        for r, lens in enumerate(reqs):
-            starts = np.concatenate([[0], np.cumsum(lens)[:-1]]).tolist()
+        for r, chunks in enumerate(reqs):
+            lens = [ln for ln, _ in chunks]
+            starts = [int(st) for _, st in chunks]
             order = torch.randperm(len(lens), generator=g).tolist()
             shuffled = [lens[o] for o in order]
             saved_starts = np.concatenate([[0], np.cumsum(shuffled)[:-1]]).tolist()
@@ -435,9 +452,10 @@ def run_ours(args):
                        "tokens_per_gpu": wl.tokens, "chunks": len(wl.chunk_len), "rope": "flexible",
                        "theta": cfg["theta"], "select": f"top{int(cfg['ratio'] * 100)}%/layer/request",
                        "scores": cfg["scores"] + (" (NCCL all-reduce over KV-head shards)" if tp else ""),
+                       "requests_per_gpu": cfg["requests"], "hit_ratio": cfg.get("hit"),
                        "parallelism": (f"tp{world}" if tp else f"dp{world}"),
                        "l2": "inputs larger than L2 (staging + paged cache >> 126 MB), no flush"},
-            "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config != 3 else None,
+            "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config in (2, 4) else None,
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -476,11 +494,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-chunks", type=int, default=4)
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2,
-                    help="BASELINE.json config: 2 (default, 8K prompt), 3 (64-request batch), 4 (70B, TP heads)")
+                    help="BASELINE.json config: 2 (default, 8K prompt), 3 (64-request batch), 4 (70B, TP heads), "
+                         "5 (Mistral-7B data-parallel hit/recompute sweep)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--hit", type=float, default=None, help="config 5: reused share of the chunks (0.5/0.75/0.95)")
+    ap.add_argument("--recompute", type=float, default=None, help="recompute ratio (top share per layer/request)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.hit is not None:
+        CONFIGS[5]["hit"] = args.hit
+    if args.recompute is not None:
+        CONFIGS[args.config]["ratio"] = args.recompute
     if args.impl == "reference":
         run_reference(args)
     else:
