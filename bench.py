@@ -344,8 +344,11 @@ def run_ours(args):
     tp = cfg["tp"]
     # data parallel: every rank loads its own requests; tensor parallel: one
     # prompt, each rank its KV-head shard
+    # --tp-shard N (config 4, one process): rank 0's KV-head shard of an N-way
+    # split, for single-GPU profiling of the TP shapes (no all-reduce)
+    shard = args.tp_shard if (tp and world == 1 and args.tp_shard) else 0
     wl = Workload(dev, seed=0 if tp else rank, config=args.config, rank=rank if tp else 0,
-                  world=world if tp else 1)
+                  world=(shard or world) if tp else 1)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -453,7 +456,8 @@ def run_ours(args):
                        "theta": cfg["theta"], "select": f"top{int(cfg['ratio'] * 100)}%/layer/request",
                        "scores": cfg["scores"] + (" (NCCL all-reduce over KV-head shards)" if tp else ""),
                        "requests_per_gpu": cfg["requests"], "hit_ratio": cfg.get("hit"),
-                       "parallelism": (f"tp{world}" if tp else f"dp{world}"),
+                       "parallelism": (f"tp{world}" if tp else f"dp{world}") +
+                                      (f" (rank-0 shard of tp{shard} on one GPU)" if shard else ""),
                        "l2": "inputs larger than L2 (staging + paged cache >> 126 MB), no flush"},
             "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config in (2, 4) else None,
             "frac_of_hbm_peak": round(value / world / peak, 4),
@@ -499,6 +503,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--hit", type=float, default=None, help="config 5: reused share of the chunks (0.5/0.75/0.95)")
     ap.add_argument("--recompute", type=float, default=None, help="recompute ratio (top share per layer/request)")
+    ap.add_argument("--tp-shard", type=int, default=0,
+                    help="config 4 on one GPU: run rank 0's KV-head shard of this TP degree (2/4/8)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
