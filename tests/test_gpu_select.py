@@ -26,10 +26,20 @@ def _scores(L, T, seed, ties=False):
 
 # long rows are split over a cluster of up to 8 CTAs (8192: eight slices of
 # 1024; 32768: eight of 4096), so ties and the k-th key straddle slices
+@pytest.fixture(params=["auto", "1", "2", "8"])
+def select_cluster(request, monkeypatch):
+    """Runs a test with the planned cluster size and with it pinned."""
+    if request.param == "auto":
+        monkeypatch.delenv("DARIC_SELECT_CLUSTER", raising=False)
+    else:
+        monkeypatch.setenv("DARIC_SELECT_CLUSTER", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("T,ratio,ties", [(512, 0.15, False), (8192, 0.15, False), (1000, 0.3, True),
                                           (33, 0.5, True), (32768, 0.2, False), (8192, 0.3, True),
                                           (20000, 0.05, True)])
-def test_topk_matches_oracle(T, ratio, ties):
+def test_topk_matches_oracle(T, ratio, ties, select_cluster):
     L, bs = 4, 16
     sc = _scores(L, T, seed=T, ties=ties)
     nblk = (T + bs - 1) // bs
@@ -80,7 +90,7 @@ def test_ragged_segments_threshold_and_edge_cases():
             np.testing.assert_array_equal(slot.cpu().numpy(), S.slots(tables[s].numpy(), exp, bs))
 
 
-def test_ragged_long_segments_split_over_a_cluster():
+def test_ragged_long_segments_split_over_a_cluster(select_cluster):
     """Segments of very different lengths in one call: the long ones set a
     cluster size of 4, the short ones leave some CTAs with empty slices."""
     bs = 16
