@@ -59,3 +59,40 @@ def test_scatter_gather_match_reference_module(ref, layout, kernel, monkeypatch)
     for n in names:
         assert torch.equal(outs["ours"][0][n].view(torch.int16), outs["ref"][0][n].view(torch.int16)), n
     assert torch.equal(outs["ours"][1], outs["ref"][1])
+
+
+def test_fused_load_outruns_reference_scatter(ref):
+    """The reference's own GPU path for the 8K-prompt load is its compiled
+    scatter_pages (then a Triton re-rotation pass per layer, not runnable
+    here). On the bench workload, the fused scatter + re-rotation must take
+    less device time than the reference scatter alone; both times are printed
+    (pytest -s)."""
+    import bench
+    wl = bench.Workload(torch.device("cuda", 0), seed=5)
+    p = wl.plan
+    rc = ref.CacheCopier()
+    for n, t in wl.kv.items():
+        rc.register_layer(n, t, False)
+    rc.register_store(wl.staging)
+    args = (p.layer_names, p.offsets.tolist(), p.byte_sizes.tolist(), p.indices_flat, p.indices_offsets.tolist())
+
+    def timed(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return sorted(ts)[len(ts) // 2]
+
+    ref_us = timed(lambda: rc.scatter_pages(*args))
+    ours_us = timed(wl.load)
+    gbs = lambda us: wl.bytes / (us * 1e-6) / 1e9
+    print(f"\nreference scatter_pages: {ref_us:.1f} us ({gbs(ref_us):.0f} GB/s, no rotation); "
+          f"fused scatter + re-rotation: {ours_us:.1f} us ({gbs(ours_us):.0f} GB/s)")
+    assert ours_us < ref_us
