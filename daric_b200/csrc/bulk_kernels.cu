@@ -23,8 +23,8 @@ namespace daric {
 namespace {
 using namespace dev;
 
-// Consumer warps per SM; a CTA has kConsumerWarps / ctas_per_sm of them plus
-// one producer warp (ctas_per_sm = 1, 2 or 4 CTAs share an SM).
+// Consumer warps of a CTA: BulkGeom::cwarps (at most kConsumerWarps, the
+// SM's warps shared by its ctas_per_sm CTAs), plus one producer warp.
 constexpr int kConsumerWarps = 16;
 constexpr int kBulkThreads = kConsumerWarps * 32 + 32;  // largest CTA
 constexpr int kMaxStages = 8;
@@ -576,7 +576,7 @@ void launch_bulk(K kernel, const PageLaunch& p, const BulkGeom& g, int sm_count,
   }
   const int64_t ctas = (int64_t)sm_count * g.ctas_per_sm;
   const int grid = (int)(p.total_units < ctas ? p.total_units : ctas);
-  const int threads = (kConsumerWarps / g.ctas_per_sm + 1) * 32;
+  const int threads = (g.cwarps + 1) * 32;
   kernel<<<grid, threads, smem, s>>>(p, g);
   DARIC_CUDA(cudaGetLastError());
 }

@@ -475,9 +475,9 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // pins 1, 2 or 4; each CTA has its own producer warp and a share of the
 // consumer warps and shared memory);
 // DARIC_BULK_CGROUPS splits the consumer warps into 2 or 4 groups.
-// DARIC_BULK_CTAS, DARIC_BULK_UNIT_PAGES, DARIC_BULK_FACTORS=l2,
-// DARIC_BULK_FACTOR_BUFFERS and DARIC_BULK_FACTOR_FORMAT=f32 pin choices for
-// A/B measurements.
+// DARIC_BULK_CTAS, DARIC_BULK_CGROUPS, DARIC_BULK_CWARPS,
+// DARIC_BULK_UNIT_PAGES, DARIC_BULK_FACTORS=l2, DARIC_BULK_FACTOR_BUFFERS and
+// DARIC_BULK_FACTOR_FORMAT=f32 pin choices for A/B measurements.
 BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, bool rotate, bool scores,
                    int tab_dtype) {
   const char* fmt = std::getenv("DARIC_BULK_FACTOR_FORMAT");
@@ -502,6 +502,7 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
   const size_t pin_unit = (size_t)env_int("DARIC_BULK_UNIT_PAGES", 1, 8);
   const long pin_ctas = env_int("DARIC_BULK_CTAS", 1, 4);
   const long pin_groups = env_int("DARIC_BULK_CGROUPS", 1, 4);
+  const long pin_cwarps = env_int("DARIC_BULK_CWARPS", 1, 16);
   const char* fv = std::getenv("DARIC_BULK_FACTORS");
   const bool allow_staged = fac > 0 && stageable && !(fv && std::strcmp(fv, "l2") == 0);
   // CTAs per SM: pages of 8 KiB or less (one KV head of 128 at block 16)
@@ -536,6 +537,15 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
       g.fac_compact = compact ? 1 : 0;
       g.ctas_per_sm = ctas;
       g.cgroups = (int32_t)groups;
+      // consumer warps: the SM's 16 shared by its CTAs; 14 for a single CTA
+      // without deviation scores, whose consumers idle part of the time and
+      // only add issue contention (measured: 2% faster; with scores the
+      // consumers are the bound and keep all 16). DARIC_BULK_CWARPS pins a
+      // count, rounded down to a multiple of the groups.
+      int cw = (ctas == 1 && !scores) ? 14 : 16 / ctas;
+      if (pin_cwarps > 0 && pin_cwarps <= 16 / ctas) cw = (int)pin_cwarps;
+      cw -= cw % (int)groups;
+      g.cwarps = cw > 0 ? cw : (int)groups;
       return true;
     };
     // The largest unit (up to the per-CTA target) that fits three stages,

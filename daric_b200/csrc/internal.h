@@ -269,7 +269,7 @@ struct BulkGeom {
   int32_t fac_compact;  // factors stored as bf16 pairs (bf16 tables) instead of fp32
   int32_t ctas_per_sm;  // 1, 2 or 4 CTAs (each with its own producer warp) per SM
   int32_t cgroups;      // consumer-warp groups (1, 2 or 4) taking alternate units
-  int32_t pad;
+  int32_t cwarps;       // consumer warps per CTA (plus one producer warp)
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).

@@ -30,7 +30,7 @@ def _setup(layout, dt, nb=24, bs=16, H=2, D=128, nlayers=2, seed=0):
 # factors stored as bf16, staged with the pages; small pages: 4 CTAs per
 # SM), with fp32 factors, with factors read from L2 in 3-page units (ragged
 # last units), with 1 and 2 CTAs per SM, with 4 consumer-warp groups, with
-# one factor buffer, and the SIMT vector kernel
+# one factor buffer, with 16 consumer warps, and the SIMT vector kernel
 _VARIANTS = {
     "bulk": {},
     "bulk-f32": {"DARIC_BULK_FACTOR_FORMAT": "f32"},
@@ -39,6 +39,7 @@ _VARIANTS = {
     "bulk-2cta": {"DARIC_BULK_CTAS": "2"},
     "bulk-4groups": {"DARIC_BULK_CGROUPS": "4"},
     "bulk-1facbuf": {"DARIC_BULK_FACTOR_BUFFERS": "1"},
+    "bulk-16warps": {"DARIC_BULK_CWARPS": "16"},
     "simt": {"DARIC_PAGE_KERNEL": "simt"},
 }
 
@@ -47,7 +48,7 @@ _VARIANTS = {
 def page_kernel(request, monkeypatch):
     """Runs a test with each page-kernel implementation."""
     for k in ("DARIC_PAGE_KERNEL", "DARIC_BULK_FACTOR_FORMAT", "DARIC_BULK_FACTORS", "DARIC_BULK_UNIT_PAGES",
-              "DARIC_BULK_CTAS", "DARIC_BULK_CGROUPS", "DARIC_BULK_FACTOR_BUFFERS"):
+              "DARIC_BULK_CTAS", "DARIC_BULK_CGROUPS", "DARIC_BULK_FACTOR_BUFFERS", "DARIC_BULK_CWARPS"):
         monkeypatch.delenv(k, raising=False)
     for k, v in _VARIANTS[request.param].items():
         monkeypatch.setenv(k, v)
