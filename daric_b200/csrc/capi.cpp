@@ -471,9 +471,9 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // shared-memory factor buffers when they fit too (else in one, loaded once
 // the units reading the previous block are done), else the consumer warps
 // read it from L2.
-// Pages of 8 KiB or less run two CTAs per SM, others one (DARIC_BULK_CTAS
-// pins 1, 2 or 4; each CTA has its own producer warp and a share of the
-// consumer warps and shared memory);
+// Small pages run 2 or 4 CTAs per SM (more with deviation scores), others
+// one (DARIC_BULK_CTAS pins 1, 2 or 4; each CTA has its own producer warp and
+// a share of the consumer warps and shared memory);
 // DARIC_BULK_CGROUPS splits the consumer warps into 2 or 4 groups.
 // DARIC_BULK_CTAS, DARIC_BULK_CGROUPS, DARIC_BULK_CWARPS,
 // DARIC_BULK_UNIT_PAGES, DARIC_BULK_FACTORS=l2, DARIC_BULK_FACTOR_BUFFERS and
@@ -505,9 +505,14 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
   const long pin_cwarps = env_int("DARIC_BULK_CWARPS", 1, 16);
   const char* fv = std::getenv("DARIC_BULK_FACTORS");
   const bool allow_staged = fac > 0 && stageable && !(fv && std::strcmp(fv, "l2") == 0);
-  // CTAs per SM: pages of 8 KiB or less (one KV head of 128 at block 16)
-  // run two CTAs per SM, so two producers feed the SM's copy engine
-  int ctas = page <= 8 * 1024 ? 2 : 1;
+  // CTAs per SM: small pages run several CTAs per SM, so several producers
+  // feed the SM's copy engine and more units are rotated at once: pages of
+  // 8 KiB or less (one KV head of 128 at block 16) two, or four when the
+  // launch writes deviation scores (consumer-bound); pages of 16 KiB or less
+  // with scores two (measured on the TP4/TP8 head shards of the 70B shape)
+  int ctas = 1;
+  if (page <= 8 * 1024) ctas = scores ? 4 : 2;
+  else if (page <= 16 * 1024 && scores) ctas = 2;
   if (pin_ctas == 1 || pin_ctas == 2 || pin_ctas == 4) ctas = (int)pin_ctas;
   for (; ctas >= 1; ctas /= 2) {
     const size_t budget =
