@@ -254,6 +254,68 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+class NvmlSampler:
+    """SM clock and clock-event reasons of one GPU sampled every ``period``
+    seconds by a host thread (NVML), for timed regions too short for
+    nvidia-smi's sampling. The GPU is found by its UUID."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device, period=0.001):
+        import threading
+        self.period = period
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nv = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            try:
+                self._h = nv.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:
+                self._h = nv.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM))
+            self._nv = nv
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((float(mhz), int(bits)))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        import threading
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
+
+    def summary(self):
+        if not self.samples:
+            return None
+        sm = [m for m, _ in self.samples]
+        reasons = sorted({nm for _, b in self.samples for bit, nm in self.REASONS.items() if b & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "source": f"NVML every {self.period * 1e3:.0f} ms during the timed region"}
+
+
 def cpu_baseline_run(wl_cpu, min_seconds=3.0, max_reps=50):
     from oracle.torch_cpu import reused_kv_step
     torch.set_num_threads(os.cpu_count() or 1)
@@ -328,12 +390,200 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _events(n):
+    return [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+
+
+def _max_over_ranks(vals, dist, dev):
+    """Element-wise max over ranks of a list of floats (every rank calls)."""
+    t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.tolist()]
+
+
+def numa_bind(device_index):
+    """Binds this process's CPU threads to the NUMA node of its GPU (from
+    sysfs), before pinned host buffers are allocated, so their pages come
+    from the GPU's node. Returns the node, or None when unknown; the
+    previous CPU mask is kept in numa_bind.saved."""
+    numa_bind.saved = os.sched_getaffinity(0)
+    try:
+        bus = torch.cuda.get_device_properties(device_index)
+        addr = f"{bus.pci_domain_id:04x}:{bus.pci_bus_id:02x}:{bus.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{addr}/numa_node").read_text().strip())
+        if node < 0:
+            return None
+        cpus = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return node
+    except Exception:
+        return None
+
+
+def time_paths(wl, dev, stream, peak, dist, reps=10):
+    """The two unfused paths a DARIC user can run, timed with CUDA events:
+      strict : strict PIC (the reference's published configuration): the
+               Adapter re-rotates every middle group of the request in place
+               by its group offset, all layers in one launch (adapter.py:118-194)
+      dropin : the unchanged store's scatter_pages, then the Adapter's
+               flexible re-rotation in place (adapter.py:196-295)
+    Each gets its algorithmic GB/s (the path's bytes / device time) and the
+    roofline of its kernels (bytes they must move / device time)."""
+    from types import SimpleNamespace
+
+    from daric_b200.adaption import Adapter, AdaptionConfig
+    from daric_b200.cache_ops import CacheCopier
+    c = wl.cfg
+    L, H, D, bs = c["layers"], wl.heads, c["head_dim"], c["block_size"]
+    ad = Adapter(AdaptionConfig(), cache_topo=wl.loader.topo)
+    ad.register_kvcaches(wl.kv)
+    for n in wl.names:
+        ad.register_rotary_embed(n, SimpleNamespace(cos_sin_cache=wl.table, rotary_dim=D, is_neox_style=True))
+    # strict: one request per wl request, groups = its chunks in prompt order
+    gps, blists, rot_tok = [], [], 0
+    for r in range(c["requests"]):
+        ms = [m for m in range(len(wl.chunk_len)) if wl.req_of[m] == r]
+        ms.sort(key=lambda m: wl.new_pos[m])
+        gp = [0] + np.cumsum([wl.chunk_len[m] for m in ms]).tolist()
+        gps.append(gp)
+        blists.append(([b for m in ms for b in wl.chunk_blocks[m]],))
+        rot_tok += sum(gp[i + 1] - gp[i] for i in range(1, len(gp) - 2))
+    k_bytes = rot_tok * L * 2 * H * D * 2  # K read + written
+    metas = [SimpleNamespace(ptr=[nw, nw + ln], saved_pos=old, block_ids=(blk,))
+             for nw, old, ln, blk in zip(wl.new_pos, wl.old_pos, wl.chunk_len, wl.chunk_blocks)]
+    copier = CacheCopier()
+    for n, t in wl.kv.items():
+        copier.register_layer(n, t, False)
+    copier.register_store(wl.staging)
+    pl = wl.plan
+
+    def strict():
+        ad.apply_rerotate_multi(gps, blists)
+
+    def dropin():
+        copier.scatter_pages(pl.c_names, pl.offsets, pl.byte_sizes, pl.indices_flat, pl.indices_offsets)
+        ad.apply_rerotate_load(metas)
+
+    out = {}
+    for name, fn in (("strict", strict), ("dropin", dropin)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ev = _events(reps)
+        for i in range(reps):
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        ms = [a.elapsed_time(b) for a, b in ev]
+        avg, mn = _max_over_ranks([sum(ms) / reps, min(ms)], dist, dev)
+        if name == "strict":
+            alg = moved = k_bytes
+        else:
+            alg = wl.bytes
+            moved = wl.bytes + sum(wl.chunk_len) * L * 2 * H * D * 2
+        out[name] = {
+            "us": round(avg * 1e3, 2), "us_min": round(mn * 1e3, 2),
+            "algorithmic_bytes": alg, "gbs": round(alg / (avg * 1e-3) / 1e9, 1),
+            "roofline": {"bound": "hbm", "moved_bytes": moved, "achieved": round(moved / (avg * 1e-3) / 1e9, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(moved / (avg * 1e-3) / 1e9 / peak, 4)}}
+    out["strict"]["rotated_tokens"] = rot_tok
+    out["strict"]["kernel"] = "bulk_inplace_kernel (DELTA, all layers, one launch)"
+    out["dropin"]["kernel"] = "bulk_pages_kernel (plain scatter) + bulk_inplace_kernel (FLEXIBLE)"
+    return out
+
+
+def run_tp(args, dist, rank, world, dev, stream, peak):
+    """BASELINE config 4 across the ranks: one 32K-token 70B-shaped prompt,
+    KV heads split over the ranks (each rank loads and rotates its heads and
+    writes partial per-token deviation scores), one NCCL all-reduce of the
+    [80, 32768] fp32 scores, then the same top-20% selection on every rank.
+    Checks: every rank's index list and slot mapping are identical (hash
+    all-gather), and rank 0's equal a numpy top-k (ties to the lower index) of
+    the all-reduced scores."""
+    import hashlib
+
+    from daric_b200.shard import allreduce_scores
+    from daric_b200.select import topk_count
+    wl = Workload(dev, seed=0, config=4, rank=rank, world=world)
+    steps = max(3, min(args.steps, 20))
+    for _ in range(3):
+        wl.load()
+        allreduce_scores(wl.scores)
+        wl.select()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for i in range(steps):
+        e[i][0].record(stream)
+        wl.load()
+        e[i][1].record(stream)
+        allreduce_scores(wl.scores)
+        e[i][2].record(stream)
+        sel = wl.select()
+        e[i][3].record(stream)
+    torch.cuda.synchronize()
+    load = sum(x[0].elapsed_time(x[1]) for x in e) / steps
+    ar = sum(x[1].elapsed_time(x[2]) for x in e) / steps
+    sl = sum(x[2].elapsed_time(x[3]) for x in e) / steps
+    step = e[0][0].elapsed_time(e[-1][3]) / steps
+    load_min = min(x[0].elapsed_time(x[1]) for x in e)
+    load_m, ar_m, sl_m, step_m = _max_over_ranks([load, ar, sl, step], dist, dev)
+    dist.barrier()
+    # identical selection on every rank
+    idx, slot, cnt = sel.idx.cpu().numpy(), sel.slot.cpu().numpy(), sel.count.cpu().numpy()
+    h = hashlib.sha256(idx.tobytes() + slot.tobytes() + cnt.tobytes()).digest()[:8]
+    mine = torch.tensor([int.from_bytes(h, "little", signed=True)], dtype=torch.int64, device=dev)
+    allh = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(allh, mine)
+    identical = len({int(x.item()) for x in allh}) == 1
+    out = None
+    if rank == 0:
+        sc = wl.scores.cpu().numpy()
+        bt = wl.block_table.cpu().numpy().astype(np.int64)
+        L, T = sc.shape
+        k = topk_count(T, wl.cfg["ratio"])
+        ok = True
+        for l in range(L):
+            u = sc[l].view(np.uint32)
+            key = np.where(u & 0x80000000, ~u, u | 0x80000000).astype(np.uint32)
+            order = np.lexsort((np.arange(T), ~key))[:k]
+            pos = np.sort(order)
+            n = int(cnt[l, 0])
+            ok = ok and n == k and np.array_equal(idx[l, :n], pos) and \
+                np.array_equal(slot[l, :n], bt[pos // 16] * 16 + pos % 16)
+        tot = wl.bytes * world
+        out = {
+            "workload": "llama3-70b-32k-tp (BASELINE config 4)", "tp": world, "kv_heads_per_rank": wl.heads,
+            "steps": steps, "us_per_prompt": round(step_m * 1e3, 2),
+            "value_gbs": round(tot / (step_m * 1e-3) / 1e9, 1),
+            "load_us": round(load_m * 1e3, 2), "load_us_min_rank0": round(load_min * 1e3, 2),
+            "per_rank_load_frac": round(wl.bytes / (load_m * 1e-3) / 1e9 / peak, 4),
+            "allreduce_us": round(ar_m * 1e3, 2), "allreduce_bytes": int(wl.scores.numel() * 4),
+            "select_us": round(sl_m * 1e3, 2),
+            "selection_identical": identical, "selection_matches_cpu_topk": bool(ok),
+            "nccl_ranks": dist.get_world_size(), "algorithmic_bytes_per_rank": wl.bytes,
+            "limiter": "load kernel" if load_m >= ar_m else "all-reduce"}
+    del wl, sel
+    torch.cuda.empty_cache()
+    dist.barrier()
+    return out
+
+
 def run_ours(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    numa = numa_bind(local)
     dist = None
     if world > 1:
         import datetime
@@ -342,6 +592,7 @@ def run_ours(args):
     from daric_b200 import _lib
     cfg = CONFIGS[args.config]
     tp = cfg["tp"]
+    peak, peak_kind = measured_peak()
     # data parallel: every rank loads its own requests; tensor parallel: one
     # prompt, each rank its KV-head shard
     # --tp-shard N (config 4, one process): rank 0's KV-head shard of an N-way
@@ -363,7 +614,7 @@ def run_ours(args):
         raise RuntimeError(f"device error bits {warm_err} during warm-up; not timing a failing path")
     barrier()
     torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = _events(args.steps)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # With scores given as input (configs 2, 3, 5) a step's selection runs on
     # a second stream after its load, beside the next step's load, as a
@@ -371,7 +622,7 @@ def run_ours(args):
     # line); scores produced by the load (config 4) keep it in line.
     overlap = cfg["scores"] != "deviation" and not args.serial_select
     sel_stream = torch.cuda.Stream(dev)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk, NvmlSampler(dev) as nvml:
         start.record(stream)
         h0 = time.perf_counter()
         for i in range(args.steps):
@@ -395,13 +646,30 @@ def run_ours(args):
     torch.cuda.synchronize()
     ms = start.elapsed_time(end)
     kern_ms = [a.elapsed_time(b) for a, b in ev]
-    t = torch.tensor([ms], device=dev)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = _max_over_ranks([ms], dist, dev)[0]
     errors = _lib.device_errors(local)
 
-    # ---- e2e: public API from pinned host buffers
+    # ---- host cost of one call with the descriptor ring free (6 steps = 12
+    # of its 16 slots, enqueued after the device went idle)
+    torch.cuda.synchronize()
+    t_load, t_sel = [], []
+    for _ in range(6):
+        a = time.perf_counter()
+        wl.load()
+        b = time.perf_counter()
+        wl.select()
+        t_load.append(b - a)
+        t_sel.append(time.perf_counter() - b)
+    torch.cuda.synchronize()
+    host_call = {"load_us": round(statistics.median(t_load) * 1e6, 1),
+                 "select_us": round(statistics.median(t_sel) * 1e6, 1),
+                 "note": "median host time per call with the descriptor ring free (no back-pressure)"}
+
+    # ---- the unfused paths (strict PIC in place, and scatter + in-place flexible)
+    paths = time_paths(wl, dev, stream, peak, dist) if not tp else None
+
+    # ---- e2e: public API from pinned host buffers; each step builds its
+    # request's load plan (block ids uploaded) as a server does per request
     from daric_b200.cache_ops import batched_memcpy_h2d
     host_shm = torch.empty(wl.staging.numel(), dtype=torch.uint8).pin_memory()
     host_shm.copy_(wl.staging)
@@ -413,11 +681,13 @@ def run_ours(args):
     chunk_off = wl.plan.chunk_offsets.tolist()
     chunk_size = wl.plan.chunk_sizes.tolist()
     e2e_steps = max(3, min(args.steps, 10))
+    block_lists = [(b,) for b in wl.chunk_blocks]
 
     def e2e_step():
         batched_memcpy_h2d(host_shm, wl.staging, chunk_off, chunk_off, chunk_size)
         if not tp:
             wl.scores.copy_(host_scores, non_blocking=True)
+        wl.plan = wl.loader.plan(block_lists)
         wl.load()
         if tp:
             from daric_b200.shard import allreduce_scores
@@ -427,30 +697,39 @@ def run_ours(args):
         out_slot.copy_(s.slot, non_blocking=True)
         out_cnt.copy_(s.count, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(local) as clk_e2e:
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        # the host->device ceiling: one plain pinned copy of the same bytes
+        # on every rank at once
+        barrier()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(3):
+            wl.staging.copy_(host_shm, non_blocking=True)
+        c1.record(stream)
+        torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    t = torch.tensor([e2e_ms, float(wl.bytes)], device=dev)
+    ceil_ms = c0.elapsed_time(c1) / 3
+    e2e_ms_max, ceil_ms_max = _max_over_ranks([e2e_ms, ceil_ms], dist, dev)
     tot_bytes = float(wl.bytes) * world
-    if dist is not None:
-        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
-        b = torch.tensor([float(wl.bytes)], device=dev)
-        dist.all_reduce(b, op=dist.ReduceOp.SUM)
-        tot_bytes = float(b.item())
-    e2e_ms_max = float(t[0].item())
     h2d = wl.staging.numel() + (0 if tp else wl.scores_host.numel() * 4)
     d2h = out_idx.numel() * 4 + out_slot.numel() * 8 + out_cnt.numel() * 4
+    del host_shm
+
+    # ---- tensor-parallel config 4 across the ranks (its one collective)
+    tp_line = run_tp(args, dist, rank, world, dev, stream, peak) if (dist is not None and not tp) else None
 
     if rank == 0:
-        peak, peak_kind = measured_peak()
         kern_avg_ms = sum(kern_ms) / len(kern_ms)
         achieved = wl.bytes / (kern_avg_ms * 1e-3) / 1e9
         traffic = None
@@ -458,6 +737,11 @@ def run_ours(args):
         if tp_file.exists() and args.config == 2:
             traffic = json.loads(tp_file.read_text()).get("rerotate_scatter_kernel_bytes_per_launch")
         value = tot_bytes * args.steps / (ms_max * 1e-3) / 1e9
+        e2e_val = tot_bytes * e2e_steps / (e2e_ms_max * 1e-3) / 1e9
+        h2d_rate = h2d * world / (e2e_ms_max / e2e_steps * 1e-3) / 1e9
+        ceiling = wl.staging.numel() * world / (ceil_ms_max * 1e-3) / 1e9
+        clocks = nvml.summary() or clk.summary()
+        clocks["reasons_whole_run"] = sorted(set(clk.summary()["reasons"]) | set(clk_e2e.summary()["reasons"]))
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
@@ -480,16 +764,28 @@ def run_ours(args):
                          "kernel_us": round(kern_avg_ms * 1e3, 2),
                          "kernel_us_min": round(min(kern_ms) * 1e3, 2),
                          "algorithmic_bytes_per_launch": wl.bytes},
-            "e2e": {"value": round(tot_bytes * e2e_steps / (e2e_ms_max * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(e2e_ms_max / e2e_steps, 4)},
+                    "ms_per_step": round(e2e_ms_max / e2e_steps, 4),
+                    "plan": "built per step (block ids uploaded per request)",
+                    "h2d_gbs": round(h2d_rate, 1),
+                    "h2d_ceiling_gbs": round(ceiling, 1),
+                    "frac_of_h2d_ceiling": round(h2d_rate / ceiling, 4),
+                    "h2d_ceiling": "plain pinned copy_ of the staging bytes on every rank at once",
+                    "numa_node": numa},
             "gpu_launches": 3 * args.steps,
             "host_us_per_step": round(host_us, 1),
-            "clocks": clk.summary(),
+            "host_us_per_call": host_call,
+            "clocks": clocks,
             "device_errors": errors,
         }
+        if paths is not None:
+            line["paths"] = paths
+        if tp_line is not None:
+            line["tp"] = tp_line
         if world == 1 and args.config == 2 and not args.no_cpu_baseline:
             sys.path.insert(0, str(ROOT))
+            os.sched_setaffinity(0, numa_bind.saved)  # the CPU baseline uses every host core
             cw, cbytes = make_cpu_workload(wl, chunks=args.cpu_chunks)
             reps, el = cpu_baseline_run(cw)
             line["cpu_baseline"] = {

@@ -21,7 +21,7 @@ OUT = PKG / "libdaric_b200.so"
 BUILD = ROOT / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES = ["capi.cpp", "page_kernels.cu", "bulk_kernels.cu", "select_kernels.cu"]
+SOURCES = ["capi.cpp", "page_kernels.cu", "bulk_kernels.cu", "inplace_kernels.cu", "select_kernels.cu"]
 
 
 def nvcc() -> str:

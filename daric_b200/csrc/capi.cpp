@@ -568,6 +568,54 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
   return BulkGeom{};
 }
 
+// Copy-engine geometry of an in-place rotation launch, or nstage = 0 when
+// the SIMT kernel runs it (DARIC_PAGE_KERNEL=simt, or a K region too large
+// for three stages). Units of up to 8 pages carry about 64 KiB of K rows;
+// K regions of 8 KiB or less run two CTAs per SM. DARIC_INPLACE_CTAS,
+// DARIC_INPLACE_CWARPS and DARIC_INPLACE_UNIT_PAGES pin the choices for A/B
+// measurements.
+InplaceGeom plan_inplace(const DeviceCtx& dc, const std::vector<LayerDev>& layers, int tab_dtype) {
+  InplaceGeom g{};
+  if (!bulk_pipeline_enabled()) return g;
+  size_t kbytes = 0;
+  for (const auto& l : layers) {
+    kbytes = std::max(kbytes, (size_t)l.nrows * (size_t)l.row_bytes);
+    // token runs must tile the K region (token-major rows, or head-major
+    // rows with whole page-size runs)
+    if (l.page_size > 65535 || l.nrows % ((int)l.tok_div.d * l.page_size) != 0) return g;
+  }
+  if (kbytes == 0 || kbytes % 16 || kbytes >= (1u << 20)) return g;
+  auto env_int = [](const char* name, long lo, long hi) -> long {
+    const char* v = std::getenv(name);
+    if (!v) return 0;
+    const long x = std::strtol(v, nullptr, 10);
+    return x >= lo && x <= hi ? x : 0;
+  };
+  int ctas = kbytes <= 8 * 1024 ? 2 : 1;
+  if (const long c = env_int("DARIC_INPLACE_CTAS", 1, 2)) ctas = (int)c;
+  int cwarps = ctas == 1 ? 16 : 8;
+  if (const long w = env_int("DARIC_INPLACE_CWARPS", 1, 16 / ctas)) cwarps = (int)w;
+  const size_t budget = std::min<size_t>((size_t)dc.smem_optin, (size_t)dc.smem_sm / (size_t)ctas - 1024);
+  const size_t pin = (size_t)env_int("DARIC_INPLACE_UNIT_PAGES", 1, 8);
+  size_t pu = pin ? pin : std::min<size_t>(8, std::max<size_t>(1, (64 * 1024) / ((size_t)ctas * kbytes)));
+  for (; pu >= 1; --pu) {
+    const size_t stage = round_up(pu * kbytes, 128);
+    const size_t ns = std::min<size_t>(8, (budget - kBulkHeader) / stage);
+    if (ns >= 3) {
+      g.nstage = (int32_t)ns;
+      g.stage_bytes = (int32_t)stage;
+      g.pages_per_unit = (int32_t)pu;
+      g.kbytes = (int32_t)kbytes;
+      g.ctas_per_sm = ctas;
+      g.cwarps = cwarps;
+      g.tab_dtype = tab_dtype;
+      return g;
+    }
+    if (pin) break;
+  }
+  return InplaceGeom{};
+}
+
 // Elements of a 16-byte vector / factors per rotation task of a layer.
 int factors_per_task(int kv_dtype, bool neox) {
   const int epv = 16 / dtype_size(kv_dtype);
@@ -1066,6 +1114,11 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
     DeviceGuard dg(L0.device);
     for (auto& grp : by_table) {
       const LayerDev& T0 = grp[0]->dev;
+      std::vector<LayerDev> ld(grp.size());
+      for (size_t l = 0; l < grp.size(); ++l) ld[l] = base_layer_dev(*grp[l]);
+      // the copy-engine pipeline reads the factors from the table itself
+      const InplaceGeom ig = plan_inplace(dc, ld, grp[0]->tab_dtype);
+      const int64_t upp = ig.nstage >= 3 ? ig.pages_per_unit : 1;
       std::vector<SegDev> segs;
       std::vector<FacJobDev> runs;
       segs.reserve(num_segs);
@@ -1089,29 +1142,31 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
         const int64_t p0 = d.tok_start / bs, p1 = (d.tok_start + d.tok_len - 1) / bs;
         DARIC_CHECK(d.blk_off + p1 < block_table_numel,
                     "segment " + std::to_string(s) + " reaches past the block table");
+        DARIC_CHECK(p1 < INT32_MAX, "segment " + std::to_string(s) + " reaches past int32 pages");
         d.first_page = (int32_t)p0;
-        d.num_units = (int32_t)(p1 - p0 + 1);
+        d.num_pages = (int32_t)(p1 - p0 + 1);
+        d.num_units = (int32_t)((d.num_pages + upp - 1) / upp);
         d.unit_begin = units;
         d.fac_tok = tok;
         units += d.num_units;
-        FacJobDev f{};
-        f.table = T0.table;
-        f.table_row = T0.table_row;
-        f.pos_a = d.pos_a;
-        f.pos_b = d.pos_b;
-        f.len = d.tok_len;
-        f.out_tok = tok;
-        f.item_begin = items;
-        f.half_rot = T0.half_rot;
-        f.P = T0.pair_vecs;
-        runs.push_back(f);
-        items += d.tok_len * (T0.half_rot / 2);
-        tok += d.tok_len;
+        if (ig.nstage < 3) {
+          FacJobDev f{};
+          f.table = T0.table;
+          f.table_row = T0.table_row;
+          f.pos_a = d.pos_a;
+          f.pos_b = d.pos_b;
+          f.len = d.tok_len;
+          f.out_tok = tok;
+          f.item_begin = items;
+          f.half_rot = T0.half_rot;
+          f.P = T0.pair_vecs;
+          runs.push_back(f);
+          items += d.tok_len * (T0.half_rot / 2);
+          tok += d.tok_len;
+        }
         segs.push_back(d);
       }
-      if (units == 0) return;
-      std::vector<LayerDev> ld(grp.size());
-      for (size_t l = 0; l < grp.size(); ++l) ld[l] = base_layer_dev(*grp[l]);
+      if (units == 0) continue;
       Blob b;
       const size_t o_l = b.add(ld.size() * sizeof(LayerDev));
       const size_t o_s = b.add(segs.size() * sizeof(SegDev));
@@ -1119,7 +1174,24 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
       Upload up(dc, b.size);
       std::memcpy(up.host() + o_l, ld.data(), ld.size() * sizeof(LayerDev));
       std::memcpy(up.host() + o_s, segs.data(), segs.size() * sizeof(SegDev));
-      std::memcpy(up.host() + o_r, runs.data(), runs.size() * sizeof(FacJobDev));
+      if (!runs.empty()) std::memcpy(up.host() + o_r, runs.data(), runs.size() * sizeof(FacJobDev));
+      InplaceLaunch p{};
+      p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_l);
+      p.num_layers = (int64_t)grp.size();
+      p.segs = reinterpret_cast<const SegDev*>(up.dev() + o_s);
+      p.num_segs = (int64_t)segs.size();
+      p.units_per_layer = units;
+      p.block_table = block_table;
+      p.block_table_numel = block_table_numel;
+      p.mode = mode;
+      p.err = dc.err_word;
+      const RotKey key{L0.kv_dtype, grp[0]->tab_dtype, L0.neox};
+      if (ig.nstage >= 3) {
+        up.send(b.size, (cudaStream_t)stream);
+        launch_bulk_inplace(p, ig, key, dc.sm_count, (cudaStream_t)stream);
+        up.finish((cudaStream_t)stream);
+        continue;
+      }
       ScratchLease lease(dc, (size_t)tok * T0.half_rot * 8, (cudaStream_t)stream);
       float4* fac = reinterpret_cast<float4*>(lease.ptr());
       up.send(b.size, (cudaStream_t)stream);
@@ -1131,19 +1203,8 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
       fl.mode = mode;
       fl.fpv = factors_per_task(L0.kv_dtype, L0.neox != 0);
       launch_factors(fl, grp[0]->tab_dtype, dc.sm_count, (cudaStream_t)stream);
-      InplaceLaunch p{};
-      p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_l);
-      p.num_layers = (int64_t)grp.size();
-      p.segs = reinterpret_cast<const SegDev*>(up.dev() + o_s);
-      p.num_segs = (int64_t)segs.size();
-      p.units_per_layer = units;
-      p.block_table = block_table;
-      p.block_table_numel = block_table_numel;
-      p.mode = mode;
-      p.err = dc.err_word;
       p.fac = fac;
-      launch_rotate_inplace(p, RotKey{L0.kv_dtype, grp[0]->tab_dtype, L0.neox}, dc.sm_count,
-                            (cudaStream_t)stream);
+      launch_rotate_inplace(p, key, dc.sm_count, (cudaStream_t)stream);
       lease.release();
       up.finish((cudaStream_t)stream);
     }

@@ -133,10 +133,21 @@ __device__ __forceinline__ uint4 pack_vec<Elem<DARIC_DTYPE_FP8_E4M3>>(const floa
   return pack<Elem<DARIC_DTYPE_FP8_E4M3>>(in);
 }
 
+// Flexible-mode combination of the old and new table entries of one
+// frequency: C = n_c*o_c + n_s*o_s, S = n_s*o_c - n_c*o_s, every product and
+// sum rounded to the table dtype (torch ops on the model-dtype table,
+// adapter.py:276-283).
+template <class T>
+__device__ __forceinline__ float2 rope_combine(float oc, float os, float nc, float ns) {
+  const float a = T::round_f(__fmul_rn(nc, oc));
+  const float b = T::round_f(__fmul_rn(ns, os));
+  const float c = T::round_f(__fmul_rn(ns, oc));
+  const float e = T::round_f(__fmul_rn(nc, os));
+  return make_float2(T::round_f(__fadd_rn(a, b)), T::round_f(__fsub_rn(c, e)));
+}
+
 // cos/sin factor of one rotary frequency `d` (fp32 result).
-//   FLEXIBLE: C = n_c*o_c + n_s*o_s, S = n_s*o_c - n_c*o_s, every product and
-//             sum rounded to the table dtype (torch ops on the model-dtype
-//             table, adapter.py:276-283).
+//   FLEXIBLE: rope_combine of table rows pa (old) and pb (new).
 //   DELTA   : C, S = table row `pa` (adapter.py:181-183).
 template <class T>
 __device__ __forceinline__ float2 rope_factor(const uint8_t* table, int64_t table_row, int half_rot, int mode,
@@ -145,13 +156,65 @@ __device__ __forceinline__ float2 rope_factor(const uint8_t* table, int64_t tabl
   const R* orow = reinterpret_cast<const R*>(table + pa * table_row);
   if (mode == DARIC_ROPE_DELTA) return make_float2(T::to_f(orow[d]), T::to_f(orow[half_rot + d]));
   const R* nrow = reinterpret_cast<const R*>(table + pb * table_row);
-  const float oc = T::to_f(orow[d]), os = T::to_f(orow[half_rot + d]);
-  const float nc = T::to_f(nrow[d]), ns = T::to_f(nrow[half_rot + d]);
-  const float a = T::round_f(__fmul_rn(nc, oc));
-  const float b = T::round_f(__fmul_rn(ns, os));
-  const float c = T::round_f(__fmul_rn(ns, oc));
-  const float e = T::round_f(__fmul_rn(nc, os));
-  return make_float2(T::round_f(__fadd_rn(a, b)), T::round_f(__fsub_rn(c, e)));
+  return rope_combine<T>(T::to_f(orow[d]), T::to_f(orow[half_rot + d]), T::to_f(nrow[d]),
+                         T::to_f(nrow[half_rot + d]));
+}
+
+// NF consecutive table entries starting at p (NF * sizeof(raw) bytes,
+// aligned to that size up to 16 bytes), widened to fp32 with vector loads
+// through the read-only cache.
+template <class T, int NF>
+__device__ __forceinline__ void load_entries(const uint8_t* p, float (&out)[NF]) {
+  using R = typename T::raw;
+  constexpr int B = NF * (int)sizeof(R);
+  union {
+    uint4 q[(B + 15) / 16];
+    uint2 h[(B + 7) / 8];
+    uint32_t w[(B + 3) / 4];
+    R r[NF];
+  } u;
+  if constexpr (B % 16 == 0) {
+#pragma unroll
+    for (int k = 0; k < B / 16; ++k) u.q[k] = __ldg(reinterpret_cast<const uint4*>(p) + k);
+  } else if constexpr (B == 8) {
+    u.h[0] = __ldg(reinterpret_cast<const uint2*>(p));
+  } else if constexpr (B == 4) {
+    u.w[0] = __ldg(reinterpret_cast<const uint32_t*>(p));
+  } else {
+#pragma unroll
+    for (int k = 0; k < NF; ++k) u.r[k] = reinterpret_cast<const R*>(p)[k];
+  }
+#pragma unroll
+  for (int k = 0; k < NF; ++k) out[k] = T::to_f(u.r[k]);
+}
+
+// Factors of frequencies [d0, d0 + NF) of one token straight from the
+// table, in the q layout of rotate_*_q with P = 1:
+//   q[g] = {C[d0+2g], C[d0+2g+1], S[d0+2g], S[d0+2g+1]}.
+// DELTA: row pa; FLEXIBLE: rope_combine of rows pa (old) and pb (new).
+// Bit-identical to rope_factor per frequency.
+template <class T, int NF>
+__device__ __forceinline__ void table_factors(const uint8_t* table, int64_t table_row, int half_rot, bool delta,
+                                              int64_t pa, int64_t pb, int d0, float4 (&q)[NF / 2]) {
+  constexpr int ES = (int)sizeof(typename T::raw);
+  const uint8_t* orow = table + pa * table_row;
+  float oc[NF], os[NF];
+  load_entries<T, NF>(orow + d0 * ES, oc);
+  load_entries<T, NF>(orow + (half_rot + d0) * ES, os);
+  if (!delta) {
+    const uint8_t* nrow = table + pb * table_row;
+    float nc[NF], ns[NF];
+    load_entries<T, NF>(nrow + d0 * ES, nc);
+    load_entries<T, NF>(nrow + (half_rot + d0) * ES, ns);
+#pragma unroll
+    for (int k = 0; k < NF; ++k) {
+      const float2 f = rope_combine<T>(oc[k], os[k], nc[k], ns[k]);
+      oc[k] = f.x;
+      os[k] = f.y;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < NF / 2; ++g) q[g] = make_float4(oc[2 * g], oc[2 * g + 1], os[2 * g], os[2 * g + 1]);
 }
 
 // Factor layout of one token (written by the factor pre-pass): the rotation
@@ -161,9 +224,33 @@ __device__ __forceinline__ float2 rope_factor(const uint8_t* table, int64_t tabl
 // so the 32 lanes of a warp (consecutive c) read consecutive 16-byte words.
 // FPV = elements per 16-byte vector (NeoX) or half of it (GPT-J).
 
+// Paired fp32 multiply (sm_100 mul.rn.f32x2), each lane rounded exactly as
+// a scalar mul.rn. The sums that follow stay scalar __fadd_rn: measured on
+// B200, the code generator contracts a paired product feeding a paired sum
+// into a fused multiply-add even with explicit .rn modifiers, while a paired
+// product feeding scalar sums stays separately rounded.
+__device__ __forceinline__ unsigned long long f2_pack(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
+  return f2_unpack(r);
+}
+
 // x1' = x1*C - x2*S ; x2' = x2*C + x1*S on NeoX halves, in fp32 with every
-// product and sum rounded separately (__fmul_rn / __fadd_rn / __fsub_rn are
-// never fused into an FMA), rounded back to the element type.
+// product and sum rounded on its own, rounded back to the element type. The
+// products run two lanes at a time (mul2_rn), the sums are scalar
+// __fadd_rn; the difference is the sum with the negated product,
+// x2*(-S) = -(x2*S) exactly, so the result is bit-identical to the scalar
+// form (no product is ever fused into an FMA).
 template <class E, bool SCORE>
 __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo, uint4& hi, float& dev) {
   constexpr int N = E::kPerVec;
@@ -173,13 +260,13 @@ __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo,
 #pragma unroll
   for (int g = 0; g < N / 2; ++g) {
     const float4 f = q[g * P];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float c = e ? f.y : f.x, s = e ? f.w : f.z;
-      const float x1 = k1[2 * g + e], x2 = k2[2 * g + e];
-      o1[2 * g + e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-      o2[2 * g + e] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-    }
+    const float2 c = make_float2(f.x, f.y), s = make_float2(f.z, f.w), ns = make_float2(-f.z, -f.w);
+    const float2 x1 = make_float2(k1[2 * g], k1[2 * g + 1]), x2 = make_float2(k2[2 * g], k2[2 * g + 1]);
+    const float2 a = mul2_rn(x1, c), b = mul2_rn(x2, ns), d = mul2_rn(x2, c), e = mul2_rn(x1, s);
+    o1[2 * g] = __fadd_rn(a.x, b.x);
+    o1[2 * g + 1] = __fadd_rn(a.y, b.y);
+    o2[2 * g] = __fadd_rn(d.x, e.x);
+    o2[2 * g + 1] = __fadd_rn(d.y, e.y);
   }
   lo = pack_vec<E>(o1);
   hi = pack_vec<E>(o2);
@@ -197,7 +284,7 @@ __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo,
 }
 
 // GPT-J: adjacent pairs (2m, 2m+1) of one vector rotate with frequency
-// c*FPV + m.
+// c*FPV + m; two pairs (frequencies 2g, 2g+1) per paired operation.
 template <class E, bool SCORE>
 __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, float& dev) {
   constexpr int N = E::kPerVec;
@@ -206,13 +293,13 @@ __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, 
 #pragma unroll
   for (int g = 0; g < N / 4; ++g) {
     const float4 f = q[g * P];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float c = e ? f.y : f.x, s = e ? f.w : f.z;
-      const float x1 = k[4 * g + 2 * e], x2 = k[4 * g + 2 * e + 1];  // (even, odd)
-      o[4 * g + 2 * e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-      o[4 * g + 2 * e + 1] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-    }
+    const float2 c = make_float2(f.x, f.y), s = make_float2(f.z, f.w), ns = make_float2(-f.z, -f.w);
+    const float2 x1 = make_float2(k[4 * g], k[4 * g + 2]), x2 = make_float2(k[4 * g + 1], k[4 * g + 3]);
+    const float2 a = mul2_rn(x1, c), b = mul2_rn(x2, ns), d = mul2_rn(x2, c), e = mul2_rn(x1, s);
+    o[4 * g] = __fadd_rn(a.x, b.x);
+    o[4 * g + 1] = __fadd_rn(d.x, e.x);
+    o[4 * g + 2] = __fadd_rn(a.y, b.y);
+    o[4 * g + 3] = __fadd_rn(d.y, e.y);
   }
   v = pack_vec<E>(o);
   if (SCORE) {

@@ -157,7 +157,9 @@ struct SegDev {
   int64_t unit_begin;  // first unit (page-slice) of the segment
   int64_t fac_tok;     // factor-buffer token of the segment's token 0
   int32_t first_page;  // tok_start / page_size
-  int32_t num_units;   // pages touched
+  int32_t num_units;   // units of the segment (SIMT: pages touched; bulk: page ranges)
+  int32_t num_pages;   // pages touched
+  int32_t pad;
 };
 
 struct InplaceLaunch {
@@ -171,6 +173,20 @@ struct InplaceLaunch {
   int32_t mode;
   int* err;
   const float4* fac;
+};
+
+// Copy-engine pipeline of the in-place rotation: NSTAGE stages of up to
+// pages_per_unit pages' K regions (kbytes each, rows at their natural
+// offsets), after the header.
+struct InplaceGeom {
+  int32_t nstage;
+  int32_t stage_bytes;
+  int32_t pages_per_unit;
+  int32_t kbytes;       // largest K region of a page in the launch
+  int32_t ctas_per_sm;
+  int32_t cwarps;       // consumer warps per CTA (plus one producer warp)
+  int32_t tab_dtype;    // rotary table dtype (factors are read from the table)
+  int32_t pad;
 };
 
 // Factor pre-pass: one run of tokens [0, len) of a chunk (or segment) with
@@ -291,6 +307,8 @@ void launch_plain_pages(const PageLaunch& p, bool gather, bool vec16, int sm_cou
 void launch_factors(const FactorLaunch& p, int tab_dtype, int sm_count, cudaStream_t s);
 void launch_rotate_scatter(const PageLaunch& p, RotKey key, int sm_count, cudaStream_t s);
 void launch_rotate_inplace(const InplaceLaunch& p, RotKey key, int sm_count, cudaStream_t s);
+// Units of InplaceLaunch are page ranges of g.pages_per_unit pages.
+void launch_bulk_inplace(const InplaceLaunch& p, const InplaceGeom& g, RotKey key, int sm_count, cudaStream_t s);
 void launch_bulk_plain(const PageLaunch& p, const BulkGeom& g, bool gather, int sm_count, cudaStream_t s);
 void launch_bulk_rotate(const PageLaunch& p, const BulkGeom& g, RotKey key, int sm_count, cudaStream_t s);
 // max_len: longest segment of the call (picks the cluster size).

@@ -420,6 +420,12 @@ namespace {
 constexpr int kNoallocMaxSegs = DARIC_NOALLOC_MAX_SEGMENTS;
 constexpr size_t kNoallocSegBytes = (size_t)kNoallocMaxSegs * sizeof(daric::SelSegDev);  // 48 KiB
 constexpr int kNoallocMaxDevices = 64;
+// Descriptors per writer launch: they travel as the writer kernel's
+// parameters (24 KiB of the 32 KiB parameter space), so a call's
+// descriptors are fixed when its launch is enqueued and no host memory is
+// read later.
+constexpr int kNoallocBatch = 512;
+static_assert(kNoallocMaxSegs % kNoallocBatch == 0, "whole writer batches");
 }  // namespace
 
 // [kNoallocMaxSegs descriptors][256 bytes: device error word]. In host code
@@ -429,10 +435,26 @@ static __device__ __align__(256) unsigned char g_select_scratch[kNoallocSegBytes
 
 namespace {
 
-std::mutex g_noalloc_mu;                              // guards the host staging and set-up
-daric::SelSegDev g_noalloc_host[kNoallocMaxSegs];     // host staging of one call's descriptors
-unsigned char* g_noalloc_dev[kNoallocMaxDevices];     // device address of the array, per device
-int g_noalloc_sms[kNoallocMaxDevices];                // SM count, per device
+struct NoallocBatch {
+  int32_t first;     // first descriptor of the batch
+  int32_t count;     // descriptors in the batch
+  int32_t clear_err; // 1: the batch also zeroes the error word
+  int32_t pad;
+  daric::SelSegDev seg[kNoallocBatch];
+};
+
+// Writes one batch of descriptors (the launch parameters) into the fixed
+// array; the first batch of a call also zeroes the error word.
+__global__ void __launch_bounds__(256) noalloc_put_descs(const __grid_constant__ NoallocBatch b) {
+  daric::SelSegDev* dst = reinterpret_cast<daric::SelSegDev*>(g_select_scratch) + b.first;
+  for (int i = threadIdx.x; i < b.count; i += blockDim.x) dst[i] = b.seg[i];
+  if (b.clear_err && threadIdx.x == 0) *reinterpret_cast<int*>(g_select_scratch + kNoallocSegBytes) = 0;
+}
+
+std::mutex g_noalloc_mu;                                // guards the set-up and the batch buffers
+NoallocBatch g_noalloc_batch[kNoallocMaxSegs / kNoallocBatch];  // host side of one call's launches
+unsigned char* g_noalloc_dev[kNoallocMaxDevices];       // device address of the array, per device
+int g_noalloc_sms[kNoallocMaxDevices];                  // SM count, per device
 
 // Set-up, once per device, with that device current: the array's device
 // address, the SM count and the kernel's dynamic shared-memory limit.
@@ -484,7 +506,7 @@ void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, i
   unsigned char* scratch = noalloc_scratch(device);
   int64_t max_len = 0;
   for (int64_t s = 0; s < num_segs; ++s) {
-    daric::SelSegDev& d = g_noalloc_host[s];
+    daric::SelSegDev& d = g_noalloc_batch[s / kNoallocBatch].seg[s % kNoallocBatch];
     d.col_off = seg_col_off[s];
     d.len = seg_len[s];
     d.pos0 = seg_pos0[s];
@@ -499,13 +521,20 @@ void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, i
     DARIC_CHECK(d.out_off + cap <= out_ld, "segment " + std::to_string(s) + " output exceeds out_ld");
     if (d.len > max_len) max_len = d.len;
   }
-  // Pageable source: the copy is staged by the driver before it returns, so
-  // the host staging can be reused by the next call right away. The error
-  // word starts at zero on every call.
-  cudaError_t e = cudaMemcpyAsync(scratch, g_noalloc_host, (size_t)num_segs * sizeof(daric::SelSegDev),
-                                  cudaMemcpyHostToDevice, stream);
-  if (e == cudaSuccess) e = cudaMemsetAsync(scratch + kNoallocSegBytes, 0, sizeof(int), stream);
-  if (e != cudaSuccess) throw Error(DARIC_ERR_CUDA, std::string("noalloc select copy: ") + cudaGetErrorString(e));
+  // The descriptors go to the device as kernel parameters (copied when the
+  // launch is enqueued), so the host buffers are free for the next call as
+  // soon as this one returns. The first batch also zeroes the error word.
+  for (int64_t b0 = 0; b0 < num_segs; b0 += kNoallocBatch) {
+    NoallocBatch& nb = g_noalloc_batch[b0 / kNoallocBatch];
+    nb.first = (int32_t)b0;
+    nb.count = (int32_t)(num_segs - b0 < kNoallocBatch ? num_segs - b0 : kNoallocBatch);
+    nb.clear_err = b0 == 0 ? 1 : 0;
+    nb.pad = 0;
+    noalloc_put_descs<<<1, 256, 0, stream>>>(nb);
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess)
+      throw Error(DARIC_ERR_CUDA, std::string("noalloc select descriptors: ") + cudaGetErrorString(le));
+  }
   daric::SelectLaunch p{};
   p.scores = scores;
   p.num_layers = num_layers;
@@ -525,7 +554,7 @@ void select_noalloc(const float* scores, int64_t num_layers, int64_t score_ld, i
   p.cluster = daric::select_cluster(num_segs * num_layers, max_len, g_noalloc_sms[device]);
   const int64_t slice = daric::select_slice(max_len, p.cluster);
   p.smem_keys = (int32_t)(slice < daric::kSmemKeys ? slice : daric::kSmemKeys);
-  e = daric::launch_select_cluster(p, stream);
+  const cudaError_t e = daric::launch_select_cluster(p, stream);
   if (e != cudaSuccess) throw Error(DARIC_ERR_CUDA, std::string("noalloc select launch: ") + cudaGetErrorString(e));
 }
 

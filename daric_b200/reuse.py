@@ -83,7 +83,15 @@ def build_load_plan(topo: CacheTopo, bpb: dict[str, int], block_ids_list: Sequen
             ids = block_ids_list[m][g]
             flat[k:k + len(ids)] = np.asarray(ids, np.int32)
             k += len(ids)
-    idx = torch.from_numpy(flat).to(device) if flat.size else torch.zeros(0, dtype=torch.int32, device=device)
+    if not flat.size:
+        idx = torch.zeros(0, dtype=torch.int32, device=device)
+    elif torch.device(device).type == "cuda":
+        # pinned source: the upload is queued on the stream instead of
+        # blocking the host (the caching host allocator keeps the buffer
+        # until the copy has run)
+        idx = torch.from_numpy(flat).pin_memory().to(device, non_blocking=True)
+    else:
+        idx = torch.from_numpy(flat).to(device)
     return LoadPlan(
         layer_names=names * M, offsets=offsets, byte_sizes=sizes.reshape(-1), indices_offsets=indices_offsets,
         indices_flat=idx, job_meta=np.repeat(np.arange(M, dtype=np.int64), L),

@@ -18,6 +18,27 @@ pytestmark = pytest.mark.gpu
 
 _TORCH = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
 
+# in-place kernel variants: the copy-engine pipeline as planned, pinned to 1
+# and 2 CTAs per SM, with 3-page units (ragged last units) and 4 consumer
+# warps, and the SIMT kernel with its factor pre-pass
+_INPLACE = {
+    "bulk": {},
+    "bulk-1cta": {"DARIC_INPLACE_CTAS": "1"},
+    "bulk-2cta": {"DARIC_INPLACE_CTAS": "2"},
+    "bulk-u3-4w": {"DARIC_INPLACE_UNIT_PAGES": "3", "DARIC_INPLACE_CWARPS": "4"},
+    "simt": {"DARIC_PAGE_KERNEL": "simt"},
+}
+
+
+@pytest.fixture(params=list(_INPLACE), autouse=True)
+def inplace_kernel(request, monkeypatch):
+    """Runs every test of this module with each in-place kernel."""
+    for k in ("DARIC_PAGE_KERNEL", "DARIC_INPLACE_CTAS", "DARIC_INPLACE_UNIT_PAGES", "DARIC_INPLACE_CWARPS"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in _INPLACE[request.param].items():
+        monkeypatch.setenv(k, v)
+    return request.param
+
 
 def _from_raw(raw, shape, dt):
     t = torch.from_numpy(raw.view(np.int16) if raw.dtype == np.uint16 else raw).reshape(shape)
@@ -138,3 +159,74 @@ def test_adapter_rereads_replaced_table():
     R.apply_rerotate_load({n: ol}, {n: R.Rotary(raw.reshape(512, 128), "bf16", 128, True)}, {n: 0}, metas)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(bytes_np(t).view(np.uint16), ol.raw)
+
+
+def _inplace_case(layout, dt, tab_dt, neox, rot_dim, mode, H=2, D=128, bs=16, seed=0):
+    """Segments of three requests (tokens of one request meet inside pages,
+    a segment inside one page, a block id 0) rotated in place over 3 layers
+    through CacheCopier.rerotate_inplace, against the oracle's rotation."""
+    from daric_b200.cache_ops import CacheCopier
+    g = torch.Generator().manual_seed(seed)
+    nb = 40
+    shape, pf = layout_shape(layout, nb, bs, H, D)
+    names = [f"model.layers.{i}.self_attn.attn" for i in range(3)]
+    kvs = {n: random_values(shape, dt, g) for n in names}
+    max_pos = 700
+    table, raw = table_tensor(max_pos, rot_dim, 5e5, tab_dt)
+    rng = np.random.default_rng(seed)
+    # request tables (positions -> blocks); request 2 uses block 0 once
+    lens_req = [80, 51, 32]  # tokens (segments below are given in tokens)
+    tables = unique_blocks(rng, nb, [(n + bs - 1) // bs for n in lens_req])
+    tables[2][-1] = 0
+    flat = np.concatenate([np.asarray(t, np.int32) for t in tables])
+    blk_off = np.concatenate([[0], np.cumsum([len(t) for t in tables])[:-1]]).astype(np.int64)
+    #        (request, start, length, pos_a, pos_b)
+    segs = [(0, 3, 21, 5, 300), (0, 24, 40, 600, 2), (0, 64, 16, 64, 64 + 7),
+            (1, 0, 35, 17, 170), (1, 35, 2, 1, 100), (2, 5, 9, 400, 33), (2, 17, 14, 31, 90)]
+    if mode == "delta":
+        segs = [(r, st, n, a, 0) for r, st, n, a, _ in segs]
+    copier = CacheCopier()
+    for n, t in kvs.items():
+        copier.register_layer(n, t, pf)
+        copier.register_rotary(n, table, rot_dim, neox)
+    ol = {n: oracle_layer(t, dt, pf)[1] for n, t in kvs.items()}
+    bt = torch.from_numpy(flat).cuda()
+    copier.rerotate_inplace(names, mode, bt, [int(blk_off[r]) for r, *_ in segs], [st for _, st, *_ in segs],
+                            [n for _, _, n, _, _ in segs], [a for *_, a, _ in segs],
+                            [b for *_, b in segs] if mode == "flexible" else None)
+    rot = R.Rotary(raw.reshape(max_pos, rot_dim), tab_dt, rot_dim, neox)
+    for r, st, n, a, b in segs:
+        idx = R.gather_index(tables[r], bs, st, n)
+        t = np.arange(n)
+        c, s = R.flexible_factors(rot, a + t, b + t) if mode == "flexible" else R.delta_factors(rot, np.full(n, a))
+        for name in names:
+            R.rotate_tokens(ol[name], rot, idx, c, s)
+    torch.cuda.synchronize()
+    assert _lib.device_errors(0) == 0
+    for n, t in kvs.items():
+        got = bytes_np(t).view(RAW_NP[dt])
+        bad = np.nonzero(got != ol[n].raw)[0]
+        assert bad.size == 0, f"{n}: {bad.size} elements differ, first at {bad[:5]}"
+
+
+@pytest.mark.parametrize("mode", ["delta", "flexible"])
+@pytest.mark.parametrize("layout", ["5d", "5dpf", "4d", "3d"])
+def test_inplace_layouts(layout, mode):
+    _inplace_case(layout, "bf16", "bf16", True, 128, mode)
+
+
+@pytest.mark.parametrize("dt,tab", [("f16", "f16"), ("f32", "f32"), ("fp8", "bf16"), ("bf16", "f32")])
+@pytest.mark.parametrize("mode", ["delta", "flexible"])
+def test_inplace_dtypes(dt, tab, mode):
+    _inplace_case("5d", dt, tab, True, 128, mode, seed=1)
+
+
+@pytest.mark.parametrize("neox,rot_dim", [(False, 128), (True, 64), (False, 64)])
+def test_inplace_gptj_and_partial_rotary(neox, rot_dim):
+    _inplace_case("5d", "bf16", "bf16", neox, rot_dim, "flexible", seed=3)
+    _inplace_case("4d", "bf16", "bf16", neox, rot_dim, "delta", seed=4)
+
+
+@pytest.mark.parametrize("H,D,bs", [(8, 128, 16), (1, 64, 16), (8, 256, 8), (4, 128, 32)])
+def test_inplace_head_shapes(H, D, bs):
+    _inplace_case("5d", "bf16", "bf16", True, D, "delta", H=H, D=D, bs=bs, seed=H + D)
