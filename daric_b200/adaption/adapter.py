@@ -169,7 +169,9 @@ class Adapter:
         dev = self.kvcaches[layer_name].device
         if flat.size == 0:
             flat = np.zeros(1, np.int32)
-        return torch.from_numpy(flat).to(dev, non_blocking=True), offs
+        # pinned source: the upload is queued on the stream, not run by the
+        # host (the caching host allocator keeps the buffer until it has run)
+        return torch.from_numpy(flat).pin_memory().to(dev, non_blocking=True), offs
 
     # --------------------------------------------------------- recompute --
     def get_recompute_length(self, group_ptr: List[int]) -> List[List[int]]:

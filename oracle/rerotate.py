@@ -126,6 +126,33 @@ def rotate_tokens(layer: KLayer, rot: Rotary, gather_idx, cos, sin, rounding: st
     return dev.astype(np.float32).sum(axis=(1, 2), dtype=np.float32)
 
 
+def rotate_dense(k_raw: np.ndarray, rot: Rotary, dtype: str, cos, sin):
+    """_fused_rerotate_kernel's math (adapter.py:30-88) on a dense block of K
+    rows: k_raw [..., T, H, D] raw elements (any leading dims, e.g. layers),
+    cos/sin [T, rotary_dim/2] fp32 factors of each token. Returns the rotated
+    raw block (RTNE to the cache dtype) and the per-token deviation
+    [..., T] = sum over heads and rotary elements of (K' - K)^2 (fp32)."""
+    _, to_f, from_f, _ = DTYPES[dtype]
+    half = rot.rotary_dim // 2
+    out = np.array(k_raw, copy=True)
+    d = np.arange(half)
+    if rot.is_neox:
+        i1, i2 = d, d + half
+    else:
+        i1, i2 = 2 * d, 2 * d + 1
+    k1 = to_f(np.ascontiguousarray(k_raw[..., i1]))
+    k2 = to_f(np.ascontiguousarray(k_raw[..., i2]))
+    c = np.asarray(cos, np.float32)[:, None, :]
+    s = np.asarray(sin, np.float32)[:, None, :]
+    o1 = (k1 * c).astype(np.float32) - (k2 * s).astype(np.float32)
+    o2 = (k2 * c).astype(np.float32) + (k1 * s).astype(np.float32)
+    r1, r2 = from_f(o1), from_f(o2)
+    out[..., i1] = r1
+    out[..., i2] = r2
+    dev = (to_f(r1) - k1) ** 2 + (to_f(r2) - k2) ** 2
+    return out, dev.astype(np.float32).sum(axis=(-2, -1), dtype=np.float32)
+
+
 def gather_index(block_ids, page_size, start, n_tok):
     """slot of positions [start, start+n_tok): block_ids[p//ps]*ps + p%ps (adapter.py:169-170)."""
     pos = np.arange(start, start + n_tok, dtype=np.int64)

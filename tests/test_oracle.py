@@ -97,3 +97,23 @@ def test_topk_matches_torch_on_distinct_scores():
     assert S.topk_positions(y, 3).tolist() == [1, 2, 4]
     assert S.topk_positions(y, 0).tolist() == []
     assert S.threshold_positions(y, 3.0).tolist() == [1, 2, 3]
+
+
+def test_rotate_dense_matches_rotate_tokens():
+    """The dense-block form of the rotation (used by the full-size GPU
+    checks) equals the per-token form on a paged layer, both styles."""
+    from oracle.numerics import f32_to_bf16
+    rng = np.random.default_rng(0)
+    T, H, D = 40, 4, 128
+    shape, strides = (2, 5, 8, H, D), (5 * 8 * H * D, 8 * H * D, H * D, D, 1)
+    kv = f32_to_bf16((rng.standard_normal(shape) * 3).astype(np.float32)).reshape(-1)
+    table = R.rope_table(600, 128, 5e5, "bf16").reshape(600, 128)
+    for neox in (True, False):
+        rot = R.Rotary(table, "bf16", 128, neox)
+        layer = R.KLayer(kv.copy(), shape, strides, False, "bf16")
+        t = np.arange(T)
+        c, s = R.flexible_factors(rot, 3 + t, 300 + t)
+        dev1 = R.rotate_tokens(layer, rot, np.arange(T), c, s)
+        out, dev2 = R.rotate_dense(kv.reshape(shape)[0].reshape(T, H, D), rot, "bf16", c, s)
+        np.testing.assert_array_equal(layer.raw.reshape(shape)[0].reshape(T, H, D), out)
+        np.testing.assert_allclose(dev1, dev2, rtol=1e-6)
