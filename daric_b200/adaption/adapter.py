@@ -48,10 +48,14 @@ def _reference_topo():
         raise RuntimeError("Adapter needs a cache topology (cache_topo=...)") from e
 
 
-def _block_list(ids) -> list[int]:
+def _block_array(ids) -> np.ndarray:
     if isinstance(ids, torch.Tensor):
-        return [int(x) for x in ids.to("cpu", torch.long).tolist()]
-    return [int(x) for x in ids]
+        return ids.to("cpu", torch.int32).numpy().reshape(-1)
+    return np.asarray(ids, dtype=np.int32).reshape(-1)
+
+
+def _block_list(ids) -> list[int]:
+    return _block_array(ids).tolist()
 
 
 class Adapter:
@@ -68,6 +72,7 @@ class Adapter:
         self.rerotate = config.rerotate
         self._copier: Optional[CacheCopier] = None
         self._table_ptr: dict[str, int] = {}
+        self._groups: dict[tuple, dict] = {}  # layer-name tuple -> {group: (names, C name array)}
 
     # ----------------------------------------------------------- registry --
     def register_kvcaches(self, kvcaches: dict[str, torch.Tensor]) -> None:
@@ -76,6 +81,7 @@ class Adapter:
         for name, t in kvcaches.items():
             self._copier.register_layer(name, t, bool(self.cache_topo.layers[name].page_first))
         self._table_ptr.clear()
+        self._groups.clear()
 
     def register_rotary_embed(self, layer_name: str, rotary_embed) -> None:
         if layer_name not in self.rotary_embeds:
@@ -95,12 +101,19 @@ class Adapter:
             self._copier.register_rotary(layer_name, table, int(rot.rotary_dim), bool(rot.is_neox_style))
             self._table_ptr[layer_name] = key
 
-    def _layers_by_group(self, names) -> dict[int, list[str]]:
-        out = defaultdict(list)
-        for n in names:
-            if n in self.kvcaches:
-                out[self.cache_topo.get_group_idx(n)].append(n)
-        return out
+    def _layers_by_group(self, names) -> dict[int, tuple]:
+        """KV group -> (layer names, their C name array), cached per name list."""
+        key = tuple(names)
+        hit = self._groups.get(key)
+        if hit is None:
+            from .._lib import names_array
+            out = defaultdict(list)
+            for n in names:
+                if n in self.kvcaches:
+                    out[self.cache_topo.get_group_idx(n)].append(n)
+            hit = {g: (ls, names_array(ls)) for g, ls in out.items()}
+            self._groups[key] = hit
+        return hit
 
     # ------------------------------------------------------------ strict --
     def apply_rerotate_multi(self, group_ptrs: List[List[int]], block_ids_list: List[tuple]) -> None:
@@ -121,13 +134,13 @@ class Adapter:
                     segs.append((req, gp[i] - base, glen, gp[i] - base))
         if not segs:
             return
-        for g_idx, layers in self._layers_by_group(self.kvcaches.keys()).items():
+        for g_idx, (layers, c_names) in self._layers_by_group(self.kvcaches.keys()).items():
             for n in layers:
                 self._sync_table(n)
             table, blk_off = self._block_table(
                 [block_ids_list[r][g_idx] for r in range(len(block_ids_list))], layers[0])
             self._copier.rerotate_inplace(
-                layers, "delta", table,
+                c_names, "delta", table,
                 seg_blk_off=[blk_off[r] for r, *_ in segs],
                 seg_tok_start=[s for _, s, _, _ in segs],
                 seg_tok_len=[n for _, _, n, _ in segs],
@@ -149,12 +162,12 @@ class Adapter:
         if not plan:
             return
         names = [layer_name] if layer_name is not None else list(self.kvcaches.keys())
-        for g_idx, layers in self._layers_by_group(names).items():
+        for g_idx, (layers, c_names) in self._layers_by_group(names).items():
             for n in layers:
                 self._sync_table(n)
             table, blk_off = self._block_table([m.block_ids[g_idx] for m, *_ in plan], layers[0])
             self._copier.rerotate_inplace(
-                layers, "flexible", table,
+                c_names, "flexible", table,
                 seg_blk_off=blk_off,
                 seg_tok_start=[0] * len(plan),
                 seg_tok_len=[c for *_, c in plan],
@@ -162,10 +175,9 @@ class Adapter:
                 seg_pos_b=[nw for _, _, nw, _ in plan])
 
     def _block_table(self, tables, layer_name: str):
-        lists = [_block_list(t) for t in tables]
-        offs = np.concatenate([[0], np.cumsum([len(x) for x in lists])[:-1]]).astype(np.int64).tolist()
-        flat = np.fromiter((b for x in lists for b in x), dtype=np.int32,
-                           count=sum(len(x) for x in lists))
+        arrs = [_block_array(t) for t in tables]
+        offs = np.concatenate([[0], np.cumsum([len(x) for x in arrs])[:-1]]).astype(np.int64).tolist()
+        flat = np.concatenate(arrs).astype(np.int32, copy=False) if arrs else np.zeros(0, np.int32)
         dev = self.kvcaches[layer_name].device
         if flat.size == 0:
             flat = np.zeros(1, np.int32)

@@ -77,75 +77,141 @@ __device__ __forceinline__ float4 as_float4(uint4 w) {
 }
 
 // Rotates the K rows of the unit's pages held in shared memory (in place).
-// Task t of the unit -> page g, row, pair c; the factors come from the
-// unit's factor block staged beside the pages (fac_staged) or straight from
-// the factor buffer in global memory (L2 resident, shared by the heads).
+// A task is (page g, token slot sl, head group hq, 16-byte column c): it
+// reads the token's factors for the column once (from the unit's factor
+// block staged beside the pages, or from the factor buffer in L2) and
+// rotates rows hq, hq + hs, ... of the token's R rows; hs head groups share
+// a token so that a full unit's tasks cover the consumer threads.
+// Consecutive lanes take consecutive columns. With scores, a token's
+// deviation is summed over its rows in registers and over the P * hs lanes
+// of its tasks by a shuffle tree; one lane stores it (0 for a token that is
+// not rotated). When those lanes do not tile a warp, the per-task sums go
+// through score_add into zeroed slots instead.
 // FC: factor entries are 4 x bf16 (8 bytes) instead of 4 x fp32 (16 bytes).
 template <class E, bool NEOX, bool SCORE, bool FC>
 __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* stage, int pages_per_unit,
                                                  const StageMeta& st, const uint8_t* fac_unit, bool fac_staged,
-                                                 int64_t len, float* tok_dev, int tid, int nthreads) {
+                                                 int64_t len, float* tok_dev, int tid, int nthreads, bool cst) {
   constexpr int ES = FC ? 8 : 16;  // bytes per factor entry
-  constexpr int U = E::kPerVec > 8 ? 1 : 2;  // fp8: 16 elements a vector, one task in flight
-  const int per_page = L.nrows * L.pair_vecs;
-  const int ntask = per_page * st.npg;
+  constexpr int NG = NEOX ? E::kPerVec / 2 : E::kPerVec / 4;  // factor entries per task
+  const int P = L.pair_vecs;
+  const int bs = L.page_size;
+  const int R = L.nrows / bs;  // rows of one token
+  // token-major rows (one run): row = sl * R + k; head-major (4-D): k * bs + sl
+  const bool tok_major = (int)L.tok_div.d == R;
+  const int sl_mul = tok_major ? R : 1, k_mul = tok_major ? 1 : bs;
+  const int per_tok = L.half_rot / 2;  // factor entries of one token
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
-  const int per_tok = L.half_rot / 2;
-  const int64_t tok_base = (int64_t)st.pl0 * L.page_size;
+  const int64_t tok_base = (int64_t)st.pl0 * bs;
   // plane-major stage: region pf of page g at (pf * pages_per_unit + g) * rbytes
   const uint32_t base = smem_addr(stage) + (uint32_t)(L.k_prefix * pages_per_unit) * (uint32_t)st.rbytes;
-  // warp-uniform trip count (score_add shuffles across the warp)
-  for (int b0 = tid; b0 - (tid & 31) < ntask; b0 += U * nthreads) {
-    uint4 lo[U], hi[U];
-    float4 q[U][E::kPerVec / 2 > 4 ? 8 : 4];
-    int off[U], slot[U];
+  const int base_tasks = st.npg * bs * P;
+  int hs = 1;
+  while (hs < R && R % (2 * hs) == 0 && base_tasks * hs < nthreads && (!SCORE || P * hs * 2 <= 32)) hs *= 2;
+  const int hshift = __ffs(hs) - 1;
+  const int ntask = base_tasks << hshift;
+  const int G = P << hshift;                        // lanes of one token
+  const bool tree = SCORE && G <= 32 && (G & (G - 1)) == 0;
+  // warp-uniform trip count (the score reduction shuffles across the warp)
+  for (int t = tid; t - (tid & 31) < ntask; t += nthreads) {
+    float dv = 0.f;
+    int slot = -1;    // unit token of this lane's task
+    bool rot = false;
+    if (t < ntask) {
+      const int tc = (int)fdiv((uint32_t)t, L.pair_div);
+      const int c = t - tc * P;
+      const int hq = tc & (hs - 1);
+      const int gs = tc >> hshift;  // unit token g * bs + sl
+      const int g = (int)fdiv((uint32_t)gs, L.tok_mod);
+      const int sl = gs - g * bs;
+      slot = gs;
+      rot = !((st.skipmask >> g) & 1) && tok_base + gs < len;
+      if (rot) {
+        float4 q[NG];
+        const uint8_t* fq = fac_unit + (gs * per_tok + c) * ES;
+        if (fac_staged) {
+          const uint32_t fa = smem_addr(fq);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int t = b0 + u * nthreads;
-      off[u] = -1;
-      slot[u] = -1;
-      if (t < ntask) {
-        const int g = (int)fdiv((uint32_t)t, L.page_div);
-        const int r = t - g * per_page;
-        const int row = (int)fdiv((uint32_t)r, L.pair_div);
-        const int c = r - row * L.pair_vecs;
-        const int sl = row_slot(L, row);
-        const int64_t tok = (int64_t)g * L.page_size + sl;  // unit token
-        if (!((st.skipmask >> g) & 1) && tok_base + tok < len) {
-          off[u] = g * st.rbytes + row * L.row_bytes + c * 16;
-          slot[u] = (int)tok;
-          lo[u] = lds128(base + off[u]);
-          if (NEOX) hi[u] = lds128(base + off[u] + hi_off);
-          const uint8_t* fq = fac_unit + ((int)tok * per_tok + c) * ES;
-          constexpr int NG = NEOX ? E::kPerVec / 2 : E::kPerVec / 4;
-          if (fac_staged) {
-            const uint32_t fa = smem_addr(fq);
+          for (int k = 0; k < NG; ++k) {
+            const uint32_t ad = fa + (uint32_t)(k * P * ES);
+            q[k] = FC ? widen_factors(lds64(ad)) : as_float4(lds128(ad));
+          }
+        } else {
 #pragma unroll
-            for (int k = 0; k < NG; ++k) {
-              const uint32_t a = fa + (uint32_t)(k * L.pair_vecs * ES);
-              q[u][k] = FC ? widen_factors(lds64(a)) : as_float4(lds128(a));
-            }
+          for (int k = 0; k < NG; ++k) {
+            const uint8_t* gp = fq + k * P * ES;
+            q[k] = FC ? widen_factors(__ldg(reinterpret_cast<const uint2*>(gp)))
+                      : __ldg(reinterpret_cast<const float4*>(gp));
+          }
+        }
+        const uint32_t cb = base + (uint32_t)(g * st.rbytes + c * 16);
+        // consumer stores: the rotated vectors go straight to the page's K
+        // region in the paged cache
+        uint8_t* gb = cst ? st.base + (int64_t)L.k_prefix * st.prefix_stride + (int64_t)st.blk[g] * st.page_stride +
+                                c * 16
+                          : nullptr;
+#pragma unroll 2
+        for (int k = hq; k < R; k += hs) {
+          const int roff = (sl * sl_mul + k * k_mul) * L.row_bytes;
+          const uint32_t ad = cb + (uint32_t)roff;
+          uint4 lo = lds128(ad), hi;
+          if (NEOX) hi = lds128(ad + hi_off);
+          if (NEOX) rotate_neox_q<E, SCORE>(q, 1, lo, hi, dv);
+          else rotate_gptj_q<E, SCORE>(q, 1, lo, dv);
+          if (cst) {
+            st_stream(gb + roff, lo);
+            if (NEOX) st_stream(gb + roff + hi_off, hi);
           } else {
-#pragma unroll
-            for (int k = 0; k < NG; ++k) {
-              const uint8_t* gp = fq + k * L.pair_vecs * ES;
-              q[u][k] = FC ? widen_factors(__ldg(reinterpret_cast<const uint2*>(gp)))
-                           : __ldg(reinterpret_cast<const float4*>(gp));
-            }
+            sts128(ad, lo);
+            if (NEOX) sts128(ad + hi_off, hi);
           }
         }
       }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      float dv = 0.f;
-      if (off[u] >= 0) {
-        if (NEOX) rotate_neox_q<E, SCORE>(q[u], 1, lo[u], hi[u], dv);
-        else rotate_gptj_q<E, SCORE>(q[u], 1, lo[u], dv);
-        sts128(base + off[u], lo[u]);
-        if (NEOX) sts128(base + off[u] + hi_off, hi[u]);
+    if (SCORE) {
+      if (tree) {
+        for (int o = 1; o < G; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+        if (slot >= 0 && ((tid & 31) & (G - 1)) == 0) tok_dev[slot] = dv;
+      } else {
+        score_add(tok_dev, rot ? slot : -1, dv);
       }
-      if (SCORE) score_add(tok_dev, slot[u], dv);
+    }
+  }
+}
+
+// Consumer-store mode: copies the unit's live regions from shared memory to
+// the paged cache with 16-byte stores, except the K vectors the rotation
+// stored itself (rotated columns of rows whose token is rotated). No
+// consumer waits for another: what is copied here is never modified.
+__device__ __forceinline__ void store_rest(const LayerDev* Lk, const StageMeta& st, const uint8_t* stage, int PU,
+                                           int tid, int nthreads) {
+  const int vecs = st.rbytes >> 4;
+  int kpf = -1, kbytes = 0;
+  bool kdone = false;  // the rotation stored the whole K region
+  int64_t tok_base = 0;
+  if (Lk != nullptr) {
+    kpf = Lk->k_prefix;
+    kbytes = Lk->nrows * Lk->row_bytes;
+    tok_base = (int64_t)st.pl0 * Lk->page_size;
+    kdone = Lk->tail_vecs == 0 && kbytes == st.rbytes && tok_base + (int64_t)st.npg * Lk->page_size <= st.len;
+  }
+  const uint32_t sbase = smem_addr(stage);
+  for (int g = 0; g < st.npg; ++g) {
+    if ((st.skipmask >> g) & 1) continue;
+    for (int pf = 0; pf < st.nreg; ++pf) {
+      const bool kreg = pf == kpf;
+      if (kreg && kdone) continue;
+      const uint32_t src = sbase + (uint32_t)((pf * PU + g) * st.rbytes);
+      uint8_t* dst = st.base + (int64_t)pf * st.prefix_stride + (int64_t)st.blk[g] * st.page_stride;
+      for (int v = tid; v < vecs; v += nthreads) {
+        const int off = v << 4;
+        if (kreg && off < kbytes) {
+          const int row = off / Lk->row_bytes;
+          const int col = (off - row * Lk->row_bytes) >> 4;
+          if (col < Lk->rot_vecs && tok_base + (int64_t)g * Lk->page_size + row_slot(*Lk, row) < st.len) continue;
+        }
+        st_stream(dst + off, lds128(src + (uint32_t)off));
+      }
     }
   }
 }
@@ -366,7 +432,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     };
     bool ok = true;
     int64_t issued = 0;  // units whose loads are armed
-    while (issued < NS - 1 && issued < n) {
+    // with bulk stores a stage is refilled once the stores of its unit have
+    // read it (NS - 1 units in flight); with consumer stores as soon as the
+    // consumers release it (NS in flight)
+    const bool cst = !GATHER && g.cstore;
+    const int inflight = cst ? NS : NS - 1;
+    while (issued < inflight && issued < n) {
       if (!issue(issued)) {
         ok = false;
         break;
@@ -391,7 +462,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       const int64_t stg_off = sm.stg_off, pstride = sm.page_stride, fstride = sm.prefix_stride;
       const int sn = sm.sn;
       float* const sout = sm.sout;
-      const bool stored = sm.npg > __popc(skipm);
+      const bool stored = !cst && sm.npg > __popc(skipm);
       if (stored) {
         // stores spread over the lanes; every lane commits a bulk group per
         // stored unit (empty for lanes without a region), so the groups of
@@ -428,8 +499,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
         for (int q = lane; q < dev_stride; q += 32) dv[q] = 0.f;
       }
       __syncwarp();
-      // the next load goes into the stage of unit i-1: its stores must have
-      // read it (unit i's group, committed last, may still be pending)
+      // the next load goes into the stage of unit i-1 (bulk stores: they must
+      // have read it; unit i's group, committed last, may still be pending)
+      // or of unit i (consumer stores)
       if (issued < n) {
         if (prev_stored) {
           if (stored) bulk_wait_read<1>(); else bulk_wait_read<0>();
@@ -454,6 +526,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   // consumers
   const int grp = warp / gwarps;
   const int gtid = tid - grp * gwarps * 32;
+  const bool cst = !GATHER && g.cstore;
   for (int64_t i = grp; i < n; i += CG) {
     const int s = (int)(i % NS);
     if (!mbar_wait(&full[s], (uint32_t)((i / NS) & 1))) {
@@ -461,15 +534,18 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       break;
     }
     const StageMeta& st = meta[s];
-    if (ROTATE && st.rot && st.npg > __popc(st.skipmask)) {
-      const LayerDev& L = p.layers[st.layer];
-      uint8_t* stage = stages + (size_t)s * g.stage_bytes;
+    const bool live = st.npg > __popc(st.skipmask);
+    uint8_t* stage = stages + (size_t)s * g.stage_bytes;
+    const LayerDev* Lk = nullptr;
+    if (ROTATE && st.rot && live) {
+      Lk = &p.layers[st.layer];
       const bool staged = g.fac_off > 0;
       const uint8_t* fac_unit = staged ? fbufs + (size_t)st.fbuf * g.fac_buf : st.fac;
-      rotate_unit_smem<E, NEOX, SCORE, FC>(L, stage, PU, st, fac_unit, staged, st.len,
-                                           devs + s * dev_stride, gtid, gwarps * 32);
-      fence_proxy_async();
+      rotate_unit_smem<E, NEOX, SCORE, FC>(*Lk, stage, PU, st, fac_unit, staged, st.len,
+                                           devs + s * dev_stride, gtid, gwarps * 32, cst);
+      if (!cst) fence_proxy_async();
     }
+    if (cst && live) store_rest(Lk, st, stage, PU, gtid, gwarps * 32);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }

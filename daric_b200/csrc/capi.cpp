@@ -500,6 +500,11 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
     return x >= lo && x <= hi ? x : 0;
   };
   const size_t pin_unit = (size_t)env_int("DARIC_BULK_UNIT_PAGES", 1, 8);
+  // Consumer stores (the consumer warps write the paged cache with 16-byte
+  // stores instead of the producer's bulk stores) only when
+  // DARIC_BULK_CSTORE=1: measured slower on the one- and two-head shards.
+  const char* cv = std::getenv("DARIC_BULK_CSTORE");
+  const bool cstore = cv && std::strcmp(cv, "1") == 0;
   const long pin_ctas = env_int("DARIC_BULK_CTAS", 1, 4);
   const long pin_groups = env_int("DARIC_BULK_CGROUPS", 1, 4);
   const long pin_cwarps = env_int("DARIC_BULK_CWARPS", 1, 16);
@@ -551,6 +556,7 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
       if (pin_cwarps > 0 && pin_cwarps <= 16 / ctas) cw = (int)pin_cwarps;
       cw -= cw % (int)groups;
       g.cwarps = cw > 0 ? cw : (int)groups;
+      g.cstore = cstore ? 1 : 0;
       return true;
     };
     // The largest unit (up to the per-CTA target) that fits three stages,

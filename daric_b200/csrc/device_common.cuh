@@ -224,33 +224,12 @@ __device__ __forceinline__ void table_factors(const uint8_t* table, int64_t tabl
 // so the 32 lanes of a warp (consecutive c) read consecutive 16-byte words.
 // FPV = elements per 16-byte vector (NeoX) or half of it (GPT-J).
 
-// Paired fp32 multiply (sm_100 mul.rn.f32x2), each lane rounded exactly as
-// a scalar mul.rn. The sums that follow stay scalar __fadd_rn: measured on
-// B200, the code generator contracts a paired product feeding a paired sum
-// into a fused multiply-add even with explicit .rn modifiers, while a paired
-// product feeding scalar sums stays separately rounded.
-__device__ __forceinline__ unsigned long long f2_pack(float2 v) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
-  return r;
-}
-__device__ __forceinline__ float2 f2_unpack(unsigned long long r) {
-  float2 v;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
-  return v;
-}
-__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
-  unsigned long long r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_pack(a)), "l"(f2_pack(b)));
-  return f2_unpack(r);
-}
-
 // x1' = x1*C - x2*S ; x2' = x2*C + x1*S on NeoX halves, in fp32 with every
-// product and sum rounded on its own, rounded back to the element type. The
-// products run two lanes at a time (mul2_rn), the sums are scalar
-// __fadd_rn; the difference is the sum with the negated product,
-// x2*(-S) = -(x2*S) exactly, so the result is bit-identical to the scalar
-// form (no product is ever fused into an FMA).
+// product and sum rounded separately (__fmul_rn / __fadd_rn / __fsub_rn are
+// never fused into an FMA), rounded back to the element type. (Paired f32x2
+// products measured slower here: the operand packing costs more moves than
+// the pairing saves, and a paired product feeding a paired sum is contracted
+// into an FMA by the code generator even with explicit .rn modifiers.)
 template <class E, bool SCORE>
 __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo, uint4& hi, float& dev) {
   constexpr int N = E::kPerVec;
@@ -260,13 +239,13 @@ __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo,
 #pragma unroll
   for (int g = 0; g < N / 2; ++g) {
     const float4 f = q[g * P];
-    const float2 c = make_float2(f.x, f.y), s = make_float2(f.z, f.w), ns = make_float2(-f.z, -f.w);
-    const float2 x1 = make_float2(k1[2 * g], k1[2 * g + 1]), x2 = make_float2(k2[2 * g], k2[2 * g + 1]);
-    const float2 a = mul2_rn(x1, c), b = mul2_rn(x2, ns), d = mul2_rn(x2, c), e = mul2_rn(x1, s);
-    o1[2 * g] = __fadd_rn(a.x, b.x);
-    o1[2 * g + 1] = __fadd_rn(a.y, b.y);
-    o2[2 * g] = __fadd_rn(d.x, e.x);
-    o2[2 * g + 1] = __fadd_rn(d.y, e.y);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float c = e ? f.y : f.x, s = e ? f.w : f.z;
+      const float x1 = k1[2 * g + e], x2 = k2[2 * g + e];
+      o1[2 * g + e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      o2[2 * g + e] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    }
   }
   lo = pack_vec<E>(o1);
   hi = pack_vec<E>(o2);
@@ -284,7 +263,7 @@ __device__ __forceinline__ void rotate_neox_q(const float4* q, int P, uint4& lo,
 }
 
 // GPT-J: adjacent pairs (2m, 2m+1) of one vector rotate with frequency
-// c*FPV + m; two pairs (frequencies 2g, 2g+1) per paired operation.
+// c*FPV + m.
 template <class E, bool SCORE>
 __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, float& dev) {
   constexpr int N = E::kPerVec;
@@ -293,13 +272,13 @@ __device__ __forceinline__ void rotate_gptj_q(const float4* q, int P, uint4& v, 
 #pragma unroll
   for (int g = 0; g < N / 4; ++g) {
     const float4 f = q[g * P];
-    const float2 c = make_float2(f.x, f.y), s = make_float2(f.z, f.w), ns = make_float2(-f.z, -f.w);
-    const float2 x1 = make_float2(k[4 * g], k[4 * g + 2]), x2 = make_float2(k[4 * g + 1], k[4 * g + 3]);
-    const float2 a = mul2_rn(x1, c), b = mul2_rn(x2, ns), d = mul2_rn(x2, c), e = mul2_rn(x1, s);
-    o[4 * g] = __fadd_rn(a.x, b.x);
-    o[4 * g + 1] = __fadd_rn(d.x, e.x);
-    o[4 * g + 2] = __fadd_rn(a.y, b.y);
-    o[4 * g + 3] = __fadd_rn(d.y, e.y);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float c = e ? f.y : f.x, s = e ? f.w : f.z;
+      const float x1 = k[4 * g + 2 * e], x2 = k[4 * g + 2 * e + 1];  // (even, odd)
+      o[4 * g + 2 * e] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+      o[4 * g + 2 * e + 1] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+    }
   }
   v = pack_vec<E>(o);
   if (SCORE) {

@@ -286,6 +286,8 @@ struct BulkGeom {
   int32_t ctas_per_sm;  // 1, 2 or 4 CTAs (each with its own producer warp) per SM
   int32_t cgroups;      // consumer-warp groups (1, 2 or 4) taking alternate units
   int32_t cwarps;       // consumer warps per CTA (plus one producer warp)
+  int32_t cstore;       // scatter: consumer warps write the paged cache (no bulk stores)
+  int32_t pad;
 };
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).

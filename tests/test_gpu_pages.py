@@ -28,9 +28,11 @@ def _setup(layout, dt, nb=24, bs=16, H=2, D=128, nlayers=2, seed=0):
 
 # page-kernel variants: the bulk-copy pipeline as planned (bf16 tables:
 # factors stored as bf16, staged with the pages; small pages: 4 CTAs per
-# SM), with fp32 factors, with factors read from L2 in 3-page units (ragged
-# last units), with 1 and 2 CTAs per SM, with 4 consumer-warp groups, with
-# one factor buffer, with 16 consumer warps, and the SIMT vector kernel
+# SM), with fp32 factors, with factors
+# read from L2 in 3-page units (ragged last units), with 1 and 2 CTAs per SM,
+# with 4 consumer-warp groups, with one factor buffer, with 16 consumer
+# warps, with consumer stores (as planned, and in 3-page units at one CTA
+# per SM), and the SIMT vector kernel
 _VARIANTS = {
     "bulk": {},
     "bulk-f32": {"DARIC_BULK_FACTOR_FORMAT": "f32"},
@@ -40,6 +42,8 @@ _VARIANTS = {
     "bulk-4groups": {"DARIC_BULK_CGROUPS": "4"},
     "bulk-1facbuf": {"DARIC_BULK_FACTOR_BUFFERS": "1"},
     "bulk-16warps": {"DARIC_BULK_CWARPS": "16"},
+    "bulk-cstore": {"DARIC_BULK_CSTORE": "1"},
+    "bulk-cstore-1cta-u3": {"DARIC_BULK_CSTORE": "1", "DARIC_BULK_CTAS": "1", "DARIC_BULK_UNIT_PAGES": "3"},
     "simt": {"DARIC_PAGE_KERNEL": "simt"},
 }
 
@@ -48,7 +52,8 @@ _VARIANTS = {
 def page_kernel(request, monkeypatch):
     """Runs a test with each page-kernel implementation."""
     for k in ("DARIC_PAGE_KERNEL", "DARIC_BULK_FACTOR_FORMAT", "DARIC_BULK_FACTORS", "DARIC_BULK_UNIT_PAGES",
-              "DARIC_BULK_CTAS", "DARIC_BULK_CGROUPS", "DARIC_BULK_FACTOR_BUFFERS", "DARIC_BULK_CWARPS"):
+              "DARIC_BULK_CTAS", "DARIC_BULK_CGROUPS", "DARIC_BULK_FACTOR_BUFFERS", "DARIC_BULK_CWARPS",
+              "DARIC_BULK_CSTORE"):
         monkeypatch.delenv(k, raising=False)
     for k, v in _VARIANTS[request.param].items():
         monkeypatch.setenv(k, v)
