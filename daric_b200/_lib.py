@@ -55,6 +55,9 @@ SIGNATURES: dict[str, tuple] = {
     "daric_copier_rerotate_scatter_pages": (
         C.c_int, [_vp, C.c_int64, C.POINTER(C.c_char_p), _i64p, _i64p, _vp, C.c_int64, C.c_int, _i64p,
                   _i64p, C.c_int, C.c_int64, _i64p, _i64p, _i64p, _vp, C.c_int64, _i64p, _i64p, _vp]),
+    "daric_copier_load_chunks": (
+        C.c_int, [_vp, C.c_int64, C.POINTER(C.c_char_p), C.c_int64, C.c_int64, C.c_int64, _i64p, _i64p, _i64p,
+                  _vp, C.c_int64, C.c_int, C.c_int, _i64p, _i64p, _i64p, _vp, C.c_int64, _i64p, _vp]),
     "daric_copier_rerotate_inplace": (
         C.c_int, [_vp, C.c_int64, C.POINTER(C.c_char_p), C.c_int, C.c_int64, _vp, C.c_int64,
                   _i64p, _i64p, _i64p, _i64p, _i64p, _vp]),

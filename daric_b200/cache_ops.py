@@ -265,6 +265,62 @@ class CacheCopier:
             jmp, code, len(pa), pap, pbp, lnp, sptr, ld, rows_p, cols_p, C.c_void_p(s)))
         del keep
 
+    def load_chunks(self, layer_names, chunk_stg_off: Sequence[int], chunk_blk_off: Sequence[int],
+                    chunk_pages: Sequence[int], block_ids: torch.Tensor, mode="flexible",
+                    pos_a: Optional[Sequence[int]] = None, pos_b: Optional[Sequence[int]] = None,
+                    chunk_len: Optional[Sequence[int]] = None, scores: Optional[torch.Tensor] = None,
+                    score_col: Optional[Sequence[int]] = None, layer_range: Optional[tuple] = None,
+                    stream: int = 0) -> None:
+        """Chunk-level fused load: the copy plan of KVIOManager._build_copy_plan
+        (gpu_kv_io.py:334-379) expanded on the device from one descriptor per
+        chunk. ``layer_names`` = every layer of a chunk in store order; chunk m
+        starts at ``chunk_stg_off[m]`` and all its layers use the block ids
+        ``block_ids[chunk_blk_off[m]:][:chunk_pages[m]]``. ``layer_range``
+        (begin, end) loads a subset of the layers. mode "flexible" / "delta" /
+        "none" with pos_a / pos_b / chunk_len per chunk as in
+        rerotate_scatter_pages; ``scores`` row j is layer j's deviations at
+        column score_col[m] + token."""
+        _check_indices(block_ids)
+        names = names_array(layer_names)
+        nl = len(names)
+        l0, l1 = layer_range if layer_range is not None else (0, nl)
+        so, sop = i64(chunk_stg_off)
+        bo, bop = i64(chunk_blk_off)
+        pg, pgp = i64(chunk_pages)
+        M = len(so)
+        if not (len(bo) == len(pg) == M):
+            raise RuntimeError("chunk arrays must have the same length")
+        code = mode_code(mode)
+        keep = []
+        pap = pbp = lnp = None
+        if code != _lib.ROPE_NONE:
+            pa, pap = i64(pos_a)
+            ln, lnp = i64(chunk_len)
+            pb, pbp = i64(pos_b if pos_b is not None else [0] * M)
+            if not (len(pa) == len(ln) == len(pb) == M):
+                raise RuntimeError("chunk position arrays must have one entry per chunk")
+            keep += [pa, ln, pb]
+        sptr, ld, colp = None, 0, None
+        if scores is not None:
+            if not scores.is_cuda or scores.dtype != torch.float32 or scores.dim() != 2 or scores.stride(1) != 1:
+                raise RuntimeError("scores must be a CUDA float32 matrix with unit column stride")
+            if score_col is None or scores.shape[0] < l1:
+                raise RuntimeError("scores need score_col and one row per layer")
+            col, colp = i64(score_col)
+            if len(col) != M:
+                raise RuntimeError("score_col must have one entry per chunk")
+            if code != _lib.ROPE_NONE and M and int((col + keep[1]).max()) > scores.shape[1]:
+                raise RuntimeError("score_col + chunk_len exceeds the score row")
+            keep.append(col)
+            sptr, ld = C.c_void_p(scores.data_ptr()), scores.stride(0)
+        dev = block_ids.device.index
+        s = _stream_ptr(stream, dev)
+        _record(block_ids, stream)
+        check(self._lib.daric_copier_load_chunks(
+            self._h, nl, names, int(l0), int(l1), M, sop, bop, pgp, C.c_void_p(block_ids.data_ptr()),
+            block_ids.numel(), dev, code, pap, pbp, lnp, sptr, ld, colp, C.c_void_p(s)))
+        del keep
+
     def rerotate_inplace(self, layer_names: Sequence[str], mode, block_table: torch.Tensor,
                          seg_blk_off: Sequence[int], seg_tok_start: Sequence[int], seg_tok_len: Sequence[int],
                          seg_pos_a: Sequence[int], seg_pos_b: Optional[Sequence[int]] = None,

@@ -298,7 +298,20 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
         const GroupDev G = p.groups[gi];
         const int64_t local = u - G.unit_begin;
         const int r = (int)(local / G.cnt);
-        const JobDev jd = p.jobs[G.j0 + (local - (int64_t)r * G.cnt)];
+        const int jl = (int)(local - (int64_t)r * G.cnt);
+        JobDev jd;
+        if (p.jobs != nullptr) {
+          jd = p.jobs[G.j0 + jl];
+        } else {  // chunk-level load: the job of (chunk, layer slot j0 + jl)
+          const LayerDev& Lj = p.layers[G.j0 + jl];
+          jd.stg_off = G.stg_off + (int64_t)G.n_sel * Lj.store_page_off;
+          jd.idx_off = G.idx_off;
+          jd.fac_tok = G.fac_tok;
+          jd.n_sel = G.n_sel;
+          jd.layer = G.j0 + jl;
+          jd.meta = G.meta;
+          jd.score_row = Lj.score_row;
+        }
         const LayerDev& L = p.layers[jd.layer];
         const int pl0 = r * PU;
         const int npg = min(PU, jd.n_sel - pl0);

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -98,8 +99,20 @@ struct DeviceCtx {
   std::mutex mu;
   unsigned next = 0;
   RingSlot slots[kRingSlots];
-  Scratch scratch;
+  // rotary-factor scratch, double-buffered so that one call's factor
+  // pre-pass (on fac_stream) can run beside the previous call's kernels
+  Scratch scratch[2];
+  unsigned scratch_next = 0;
+  cudaStream_t fac_stream = nullptr;
+  cudaEvent_t fac_done[2] = {nullptr, nullptr};
+  cudaEvent_t caller_mark = nullptr;
+  uint64_t table_gen_seen = 0;  // rotary-table generation the factor stream has waited for
 };
+
+// Bumped by every register_rotary: the next factor pre-pass on a device
+// first waits for all earlier work on its caller's stream (a table may
+// have just been written there).
+std::atomic<uint64_t> g_table_gen{1};
 
 std::mutex g_ctx_mu;
 std::map<int, std::unique_ptr<DeviceCtx>> g_ctx;
@@ -124,8 +137,13 @@ DeviceCtx& device_ctx(int device) {
     DARIC_CUDA(cudaMalloc((void**)&s.dev, kSlotBytes));
     s.cap = kSlotBytes;
   }
-  DARIC_CUDA(cudaEventCreateWithFlags(&c->scratch.last, cudaEventDisableTiming));
+  for (int i = 0; i < 2; ++i) {
+    DARIC_CUDA(cudaEventCreateWithFlags(&c->scratch[i].last, cudaEventDisableTiming));
+    DARIC_CUDA(cudaEventCreateWithFlags(&c->fac_done[i], cudaEventDisableTiming));
+  }
+  DARIC_CUDA(cudaEventCreateWithFlags(&c->caller_mark, cudaEventDisableTiming));
   DARIC_CUDA(cudaStreamCreateWithFlags(&c->up_stream, cudaStreamNonBlocking));
+  DARIC_CUDA(cudaStreamCreateWithFlags(&c->fac_stream, cudaStreamNonBlocking));
   auto& ref = *c;
   g_ctx[device] = std::move(c);
   return ref;
@@ -177,6 +195,10 @@ class Upload {
     side_sent_ = true;
     DARIC_CUDA(cudaStreamWaitEvent(s, slot_->sent, 0));
   }
+  // Another stream that reads the uploaded descriptors waits for them too.
+  void also_wait(cudaStream_t other) {
+    if (side_sent_) DARIC_CUDA(cudaStreamWaitEvent(other, slot_->sent, 0));
+  }
   void finish(cudaStream_t s) {
     DARIC_CUDA(cudaEventRecord(slot_->done, s));
     slot_->pending = true;
@@ -201,7 +223,7 @@ class Upload {
 // reallocates.
 class ScratchLease {
  public:
-  ScratchLease(DeviceCtx& c, size_t bytes, cudaStream_t s) : sc_(c.scratch), lock_(c.scratch.mu), s_(s) {
+  ScratchLease(DeviceCtx& c, size_t bytes, cudaStream_t s) : sc_(c.scratch[0]), lock_(c.scratch[0].mu), s_(s) {
     if (sc_.cap < bytes) {
       if (sc_.used) DARIC_CUDA(cudaEventSynchronize(sc_.last));
       if (sc_.ptr) DARIC_CUDA(cudaFree(sc_.ptr));
@@ -224,6 +246,70 @@ class ScratchLease {
   Scratch& sc_;
   std::lock_guard<std::mutex> lock_;
   cudaStream_t s_;
+};
+
+// The rotary-factor pre-pass of one call. Outside stream capture it runs on
+// the device's factor stream, so it overlaps the kernels still running on
+// the caller's stream (the previous call's load): it takes the scratch
+// buffer the call before the previous one used, the factor stream waits
+// (on the GPU) for that buffer's last reader and for the descriptor upload,
+// and the caller's stream waits for the factors before the page kernel.
+// The first pre-pass after a rotary table was (re)registered also waits
+// for all earlier work on the caller's stream. Under capture everything
+// stays on the caller's stream.
+class FactorPass {
+ public:
+  FactorPass(DeviceCtx& c, size_t bytes, cudaStream_t s) : c_(c), s_(s) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    DARIC_CUDA(cudaStreamIsCapturing(s, &cap));
+    side_ = cap == cudaStreamCaptureStatusNone;
+    fs_ = side_ ? c.fac_stream : s;
+    {
+      std::lock_guard<std::mutex> g(c.mu);
+      idx_ = (int)(c.scratch_next++ % 2);
+      const uint64_t gen = g_table_gen.load();
+      if (side_ && c.table_gen_seen != gen) {
+        DARIC_CUDA(cudaEventRecord(c.caller_mark, s));
+        DARIC_CUDA(cudaStreamWaitEvent(fs_, c.caller_mark, 0));
+        c.table_gen_seen = gen;
+      }
+    }
+    sc_ = &c.scratch[idx_];
+    lock_ = std::unique_lock<std::mutex>(sc_->mu);
+    if (sc_->cap < bytes) {
+      if (sc_->used) DARIC_CUDA(cudaEventSynchronize(sc_->last));
+      if (sc_->ptr) DARIC_CUDA(cudaFree(sc_->ptr));
+      sc_->ptr = nullptr;
+      const size_t cap2 = std::max(bytes, sc_->cap * 2);
+      sc_->cap = 0;
+      DARIC_CUDA(cudaMalloc((void**)&sc_->ptr, cap2));
+      sc_->cap = cap2;
+    } else if (sc_->used) {
+      DARIC_CUDA(cudaStreamWaitEvent(fs_, sc_->last, 0));
+    }
+  }
+  uint8_t* ptr() const { return sc_->ptr; }
+  cudaStream_t stream() const { return fs_; }
+  // after the factor kernel: the caller's stream waits for it
+  void launched() {
+    if (!side_) return;
+    DARIC_CUDA(cudaEventRecord(c_.fac_done[idx_], fs_));
+    DARIC_CUDA(cudaStreamWaitEvent(s_, c_.fac_done[idx_], 0));
+  }
+  // after the page kernel: the buffer's last reader
+  void release() {
+    DARIC_CUDA(cudaEventRecord(sc_->last, s_));
+    sc_->used = true;
+  }
+
+ private:
+  DeviceCtx& c_;
+  cudaStream_t s_;
+  cudaStream_t fs_ = nullptr;
+  bool side_ = false;
+  int idx_ = 0;
+  Scratch* sc_ = nullptr;
+  std::unique_lock<std::mutex> lock_;
 };
 
 // Lays out [section 0 | section 1 | ...] with 16-byte aligned sections.
@@ -763,10 +849,11 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   if (!metas.empty()) std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
   if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
   if (!groups.empty()) std::memcpy(up.host() + o_groups, groups.data(), groups.size() * sizeof(GroupDev));
-  std::unique_ptr<ScratchLease> lease;
-  if (fac_bytes > 0) lease = std::make_unique<ScratchLease>(dc, (size_t)fac_bytes, stream);
+  std::unique_ptr<FactorPass> lease;
+  if (fac_bytes > 0) lease = std::make_unique<FactorPass>(dc, (size_t)fac_bytes, stream);
   float4* fac = lease ? reinterpret_cast<float4*>(lease->ptr()) : nullptr;
   up.send(b.size, stream);
+  if (lease) up.also_wait(lease->stream());
   if (!runs.empty()) {
     FactorLaunch fl{};
     fl.jobs = reinterpret_cast<const FacJobDev*>(up.dev() + o_runs);
@@ -776,8 +863,9 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
     fl.mode = mode;
     fl.fpv = factors_per_task(key.kv_dtype, key.neox != 0);
     fl.compact = compact ? 1 : 0;
-    launch_factors(fl, key.tab_dtype, dc.sm_count, stream);
+    launch_factors(fl, key.tab_dtype, dc.sm_count, lease->stream());
   }
+  if (lease) lease->launched();
   PageLaunch p{};
   p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_layers);
   p.jobs = reinterpret_cast<const JobDev*>(up.dev() + o_jobs);
@@ -817,6 +905,230 @@ void do_copy(daric_copier* c, bool gather, int64_t num_jobs, const char* const* 
   for (int64_t i = 0; i < num_jobs; ++i) all[i] = i;
   run_page_jobs(c, jp, all, offsets, indices_flat, indices_numel, indices_offsets, gather, false,
                 DARIC_ROPE_NONE, nullptr, {}, nullptr, 0, nullptr, RotKey{}, (cudaStream_t)stream);
+}
+
+// Chunk-level load (daric_copier_load_chunks): chunk m holds, for every
+// layer of `names` in order, [prefix][n_sel pages][page bytes] at
+// chunk_stg_off[m] + n_sel * (bytes per page of the layers before it); the
+// call loads layers [l0, l1). All layers of a chunk use the chunk's one
+// block-id list. The bulk pipeline derives each (chunk, layer) job on the
+// device from one descriptor per chunk; the SIMT kernels get a job table
+// built here (its entries share the chunk's block-id range).
+void run_chunk_load(daric_copier* c, int64_t num_layers, const char* const* names, int64_t l0, int64_t l1,
+                    int64_t M, const int64_t* chunk_stg_off, const int64_t* chunk_blk_off,
+                    const int64_t* chunk_pages, const int32_t* block_ids, int64_t block_ids_numel,
+                    int block_ids_device, int mode, const int64_t* pos_a, const int64_t* pos_b,
+                    const int64_t* len, float* scores, int64_t score_ld, const int64_t* score_col,
+                    cudaStream_t stream) {
+  DARIC_CHECK(c != nullptr, "copier is NULL");
+  DARIC_CHECK(c->has_store, "store buffer not registered; call register_store() first");
+  DARIC_CHECK(mode == DARIC_ROPE_FLEXIBLE || mode == DARIC_ROPE_DELTA || mode == DARIC_ROPE_NONE,
+              "unknown rotation mode " + std::to_string(mode));
+  DARIC_CHECK(num_layers >= 0 && M >= 0, "negative layer or chunk count");
+  DARIC_CHECK(0 <= l0 && l0 <= l1 && l1 <= num_layers, "layer range outside the layer list");
+  if (M == 0 || l0 == l1) return;
+  DARIC_CHECK(names && chunk_stg_off && chunk_blk_off && chunk_pages, "chunk arrays must not be NULL");
+  DARIC_CHECK(block_ids != nullptr || block_ids_numel == 0, "block_ids is NULL");
+  const bool rotate = mode != DARIC_ROPE_NONE;
+  if (rotate) DARIC_CHECK(pos_a && len && (mode != DARIC_ROPE_FLEXIBLE || pos_b), "chunk position arrays are NULL");
+  if (scores) DARIC_CHECK(score_col && score_ld >= 0, "scores need score_col and a non-negative score_ld");
+  // layers: all of them fix the store layout; [l0, l1) are loaded
+  std::vector<LayerHost*> all(num_layers);
+  std::vector<int64_t> page_off(num_layers + 1, 0);
+  for (int64_t j = 0; j < num_layers; ++j) {
+    all[j] = &find_layer(c, names[j]);
+    const int64_t per_page = checked_mul(all[j]->prefix_size, all[j]->suffix, "bytes per page");
+    page_off[j + 1] = page_off[j] + per_page;
+  }
+  const int device = all[l0]->device;
+  DARIC_CHECK(block_ids_device == device, "block_ids must be on the same device as kvcache");
+  DARIC_CHECK(c->store_device == device, "store buffer must be on the same device as kvcache");
+  std::vector<LayerDev> layers;
+  bool vec16 = ((uintptr_t)c->store % 16) == 0;
+  for (int64_t j = l0; j < l1; ++j) {
+    LayerHost& L = *all[j];
+    DARIC_CHECK(L.device == device, "all layers must be on the same device; layer " + L.name);
+    DARIC_CHECK(!rotate || L.has_rot, "layer has no rotary table (register_rotary): " + L.name);
+    DARIC_CHECK(!rotate || (L.kv_dtype == all[l0]->kv_dtype && L.tab_dtype == all[l0]->tab_dtype &&
+                            L.neox == all[l0]->neox),
+                "load_chunks: the layers of one call must share KV dtype, table dtype and rotary style");
+    LayerDev d = base_layer_dev(L);
+    d.store_page_off = page_off[j];
+    d.score_row = scores ? (int32_t)j : -1;
+    if (L.suffix % 16 || L.page_stride % 16 || L.prefix_stride % 16 || ((uintptr_t)L.data % 16)) vec16 = false;
+    layers.push_back(d);
+  }
+  // chunks
+  std::vector<MetaDev> metas(M);
+  for (int64_t m = 0; m < M; ++m) {
+    const int64_t ns = chunk_pages[m];
+    DARIC_CHECK(ns >= 0 && ns <= INT32_MAX, "bad page count at chunk " + std::to_string(m));
+    DARIC_CHECK(chunk_stg_off[m] >= 0 && chunk_blk_off[m] >= 0, "negative chunk offset at chunk " + std::to_string(m));
+    DARIC_CHECK(chunk_blk_off[m] + ns <= block_ids_numel, "chunk " + std::to_string(m) + " reaches past block_ids");
+    const int64_t bytes = checked_mul(ns, page_off[num_layers], "chunk bytes");
+    DARIC_CHECK(chunk_stg_off[m] <= c->store_bytes && bytes <= c->store_bytes - chunk_stg_off[m],
+                "store range out of bounds at chunk " + std::to_string(m));
+    if (chunk_stg_off[m] % 16) vec16 = false;
+    MetaDev& d = metas[m];
+    d.pos_a = rotate ? pos_a[m] : 0;
+    d.pos_b = mode == DARIC_ROPE_FLEXIBLE ? pos_b[m] : 0;
+    d.len = rotate ? len[m] : 0;
+    DARIC_CHECK(d.len >= 0, "negative chunk length at chunk " + std::to_string(m));
+    d.score_col = scores ? score_col[m] : 0;
+    if (scores) DARIC_CHECK(d.score_col >= 0, "negative score column at chunk " + std::to_string(m));
+    d.rotate = (!rotate || d.len == 0 || (mode == DARIC_ROPE_FLEXIBLE && d.pos_a == d.pos_b)) ? 0 : 1;
+  }
+  if (vec16) {
+    for (int64_t j = 0; j < num_layers; ++j)
+      if ((all[j]->prefix_size * all[j]->suffix) % 16) vec16 = false;
+  }
+  DARIC_CHECK(vec16 || !rotate, "load_chunks needs 16-byte aligned layers, chunk offsets and pages");
+  DeviceCtx& dc = device_ctx(device);
+  const RotKey key = rotate ? RotKey{all[l0]->kv_dtype, all[l0]->tab_dtype, all[l0]->neox} : RotKey{};
+  bool uniform = true;  // one group per chunk needs one page size / rotary geometry
+  for (const auto& d : layers)
+    uniform = uniform && d.page_size == layers[0].page_size && d.half_rot == layers[0].half_rot &&
+              d.has_rot == layers[0].has_rot && d.table == layers[0].table;
+  const BulkGeom bg = (vec16 && uniform && bulk_pipeline_enabled())
+                          ? plan_bulk(dc, layers, rotate, rotate && scores, key.tab_dtype)
+                          : BulkGeom{};
+  const bool bulk = bg.nstage >= 3;
+  const int64_t upp = bulk ? bg.pages_per_unit : 1;
+  const bool compact = bulk && bg.fac_compact;
+  const int64_t Lc = l1 - l0;
+  // factor runs: one per rotating chunk and table, padded to whole pages
+  std::vector<FacJobDev> runs;
+  std::vector<int64_t> fac_tok(M, 0);
+  int64_t items = 0, fac_bytes = 0;
+  std::vector<std::pair<const void*, int64_t>> tables;  // (table, first run) per distinct table
+  for (size_t li = 0; li < layers.size() && rotate; ++li) {
+    const LayerDev& L = layers[li];
+    bool seen = false;
+    for (auto& t : tables) seen = seen || t.first == (const void*)L.table;
+    if (seen) continue;
+    DARIC_CHECK(tables.empty(), "load_chunks: the layers of one call must share one rotary table");
+    tables.emplace_back((const void*)L.table, 0);
+    const int64_t tok_bytes = (int64_t)token_factor_bytes(L.half_rot, compact);
+    for (int64_t m = 0; m < M; ++m) {
+      if (!metas[m].rotate) continue;
+      const int64_t ntok = chunk_pages[m] * L.page_size;
+      const int64_t ln = std::min(metas[m].len, ntok);
+      const MetaDev& md = metas[m];
+      const bool ok = mode == DARIC_ROPE_FLEXIBLE
+                          ? (md.pos_a >= 0 && md.pos_b >= 0 && md.pos_a + ln <= L.max_pos && md.pos_b + ln <= L.max_pos)
+                          : (md.pos_a >= 0 && md.pos_a < L.max_pos);
+      DARIC_CHECK(ln <= 0 || ok, "rotary position out of range of cos_sin_cache (max_position=" +
+                                     std::to_string(L.max_pos) + ") at chunk " + std::to_string(m));
+      FacJobDev f{};
+      f.table = L.table;
+      f.table_row = L.table_row;
+      f.pos_a = md.pos_a;
+      f.pos_b = md.pos_b;
+      f.len = ln;
+      f.half_rot = L.half_rot;
+      f.P = L.pair_vecs;
+      f.out_tok = (fac_bytes + tok_bytes - 1) / tok_bytes;
+      f.item_begin = items;
+      items += ln * (L.half_rot / 2);
+      fac_bytes = (f.out_tok + ntok) * tok_bytes;
+      fac_tok[m] = f.out_tok;
+      if (ln > 0) runs.push_back(f);
+    }
+  }
+  // groups (bulk: one per chunk, jobs derived on the device) or a job table
+  std::vector<GroupDev> groups;
+  std::vector<JobDev> jobs;
+  int64_t units = 0;
+  for (int64_t m = 0; m < M; ++m) {
+    const int64_t ns = chunk_pages[m];
+    if (ns == 0) continue;
+    if (bulk) {
+      GroupDev gd{};
+      gd.unit_begin = units;
+      gd.j0 = 0;
+      gd.cnt = (int32_t)Lc;
+      gd.n_sel = (int32_t)ns;
+      gd.nranges = (int32_t)((ns + upp - 1) / upp);
+      gd.stg_off = chunk_stg_off[m];
+      gd.idx_off = chunk_blk_off[m];
+      gd.fac_tok = fac_tok[m];
+      gd.meta = (int32_t)m;
+      units += (int64_t)gd.nranges * Lc;
+      groups.push_back(gd);
+    } else {
+      for (int64_t li = 0; li < Lc; ++li) {
+        JobDev j{};
+        j.stg_off = chunk_stg_off[m] + ns * layers[li].store_page_off;
+        j.idx_off = chunk_blk_off[m];
+        j.unit_begin = units;
+        j.fac_tok = fac_tok[m];
+        j.n_sel = (int32_t)ns;
+        j.layer = (int32_t)li;
+        j.meta = rotate ? (int32_t)m : -1;
+        j.score_row = (rotate && scores) ? layers[li].score_row : -1;
+        jobs.push_back(j);
+        units += ns;
+      }
+    }
+  }
+  if (units == 0) return;
+  DeviceGuard dg(device);
+  Blob b;
+  const size_t o_layers = b.add(layers.size() * sizeof(LayerDev));
+  const size_t o_jobs = b.add(jobs.size() * sizeof(JobDev));
+  const size_t o_metas = b.add(metas.size() * sizeof(MetaDev));
+  const size_t o_runs = b.add(runs.size() * sizeof(FacJobDev));
+  const size_t o_groups = b.add(groups.size() * sizeof(GroupDev));
+  Upload up(dc, b.size);
+  std::memcpy(up.host() + o_layers, layers.data(), layers.size() * sizeof(LayerDev));
+  if (!jobs.empty()) std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
+  std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
+  if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
+  if (!groups.empty()) std::memcpy(up.host() + o_groups, groups.data(), groups.size() * sizeof(GroupDev));
+  std::unique_ptr<FactorPass> lease;
+  if (fac_bytes > 0) lease = std::make_unique<FactorPass>(dc, (size_t)fac_bytes, stream);
+  float4* fac = lease ? reinterpret_cast<float4*>(lease->ptr()) : nullptr;
+  up.send(b.size, stream);
+  if (lease) up.also_wait(lease->stream());
+  if (!runs.empty()) {
+    FactorLaunch fl{};
+    fl.jobs = reinterpret_cast<const FacJobDev*>(up.dev() + o_runs);
+    fl.num_jobs = (int64_t)runs.size();
+    fl.total_items = items;
+    fl.out = fac;
+    fl.mode = mode;
+    fl.fpv = factors_per_task(key.kv_dtype, key.neox != 0);
+    fl.compact = compact ? 1 : 0;
+    launch_factors(fl, key.tab_dtype, dc.sm_count, lease->stream());
+  }
+  if (lease) lease->launched();
+  PageLaunch p{};
+  p.layers = reinterpret_cast<const LayerDev*>(up.dev() + o_layers);
+  p.jobs = bulk ? nullptr : reinterpret_cast<const JobDev*>(up.dev() + o_jobs);
+  p.metas = reinterpret_cast<const MetaDev*>(up.dev() + o_metas);
+  p.store = c->store;
+  p.store_mut = c->store;
+  p.indices = block_ids;
+  p.indices_numel = block_ids_numel;
+  p.num_jobs = (int64_t)jobs.size();
+  p.total_units = units;
+  p.mode = mode;
+  p.scores = rotate ? scores : nullptr;
+  p.score_ld = score_ld;
+  p.err = dc.err_word;
+  p.fac = fac;
+  p.groups = reinterpret_cast<const GroupDev*>(up.dev() + o_groups);
+  p.num_groups = (int64_t)groups.size();
+  if (bulk) {
+    if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
+    else launch_bulk_plain(p, bg, false, dc.sm_count, stream);
+  } else if (rotate) {
+    launch_rotate_scatter(p, key, dc.sm_count, stream);
+  } else {
+    launch_plain_pages(p, false, vec16, dc.sm_count, stream);
+  }
+  if (lease) lease->release();
+  up.finish(stream);
 }
 
 // Rotation geometry of a registered layer (adapter.py:311-368 stride rules).
@@ -995,6 +1307,7 @@ int daric_copier_register_rotary(daric_copier* c, const char* layer_name, int kv
     DARIC_CHECK(c, "copier is NULL");
     LayerHost& L = find_layer(c, layer_name);
     resolve_rotary(L, kv_dtype, table, tab_dtype, max_pos, rot_dim, is_neox);
+    g_table_gen.fetch_add(1);
   });
 }
 
@@ -1075,6 +1388,20 @@ int daric_copier_rerotate_scatter_pages(
                       DARIC_ROPE_NONE, nullptr, {}, nullptr, 0, nullptr, RotKey{}, (cudaStream_t)stream);
       }
     }
+  });
+}
+
+int daric_copier_load_chunks(daric_copier* c, int64_t num_layers, const char* const* layer_names,
+                             int64_t layer_begin, int64_t layer_end, int64_t num_chunks,
+                             const int64_t* chunk_stg_off, const int64_t* chunk_blk_off,
+                             const int64_t* chunk_pages, const int32_t* block_ids, int64_t block_ids_numel,
+                             int block_ids_device, int mode, const int64_t* pos_a, const int64_t* pos_b,
+                             const int64_t* len, float* scores, int64_t score_ld, const int64_t* score_col,
+                             void* stream) {
+  return guarded([&] {
+    run_chunk_load(c, num_layers, layer_names, layer_begin, layer_end, num_chunks, chunk_stg_off, chunk_blk_off,
+                   chunk_pages, block_ids, block_ids_numel, block_ids_device, mode, pos_a, pos_b, len, scores,
+                   score_ld, score_col, (cudaStream_t)stream);
   });
 }
 

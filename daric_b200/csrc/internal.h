@@ -96,6 +96,10 @@ struct LayerDev {
   const uint8_t* table;   // cos_sin_cache
   int64_t table_row;      // bytes per table row
   int64_t max_pos;        // rows of the table
+  // chunk-level loads (daric_copier_load_chunks)
+  int64_t store_page_off; // bytes per chunk page of the layers before this one in the store
+  int32_t score_row;      // score row of the layer (-1 = no scores)
+  int32_t pad2;
 };
 
 struct JobDev {
@@ -141,11 +145,20 @@ struct PageLaunch {
 // count and factor run form a group; its units go page range by page range
 // and, within a range, job by job (unit = range r of job j0 + l at
 // unit_begin + r * cnt + l), so consecutive units share their factor block.
+// Chunk-level loads (PageLaunch::jobs == nullptr): a group is one chunk and
+// its jobs are the launch's layers [j0, j0 + cnt) (layer-table slots); job
+// (chunk, layer l) reads the store at stg_off + n_sel * store_page_off(l)
+// and the chunk's block ids at idx_off, for every layer.
 struct GroupDev {
   int64_t unit_begin;
   int32_t j0, cnt;     // jobs [j0, j0 + cnt)
   int32_t n_sel;       // pages of each job
   int32_t nranges;     // ceil(n_sel / pages_per_unit)
+  int64_t stg_off;     // chunk-level: store offset of the chunk
+  int64_t idx_off;     // chunk-level: first block id of the chunk
+  int64_t fac_tok;     // chunk-level: factor-buffer token of the chunk's token 0
+  int32_t meta;        // chunk-level: chunk index
+  int32_t pad;
 };
 
 // In-place rotation segments.

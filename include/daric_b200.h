@@ -160,6 +160,29 @@ DARIC_API int daric_copier_rerotate_scatter_pages(
     const int64_t* meta_pos_a, const int64_t* meta_pos_b, const int64_t* meta_len, float* scores,
     int64_t score_ld, const int64_t* job_score_row, const int64_t* meta_score_col, void* stream);
 
+/* Chunk-level fused load: the copy plan of KVIOManager._build_copy_plan
+ * (management/service/gpu_kv_io.py:334-379: per chunk, per layer, offsets,
+ * byte sizes and a block-id list repeated for every layer) built on the
+ * device from one descriptor per chunk. layer_names lists every layer of a
+ * chunk in store order (the store's sorted layer order,
+ * gpu_kv_io.py:355-373); chunk m's region at chunk_stg_off[m] holds, for
+ * layer j, [prefix][chunk_pages[m] pages][page bytes] after the layers
+ * before it (chunk_pages[m] x their bytes per page). Every layer of chunk m
+ * uses the block ids block_ids[chunk_blk_off[m] .. + chunk_pages[m])
+ * (device int32). The call loads layers [layer_begin, layer_end) only
+ * (layer-wise loading). mode, pos_a/pos_b/len per chunk as meta_* of
+ * daric_copier_rerotate_scatter_pages (DARIC_ROPE_NONE: plain scatter);
+ * with scores, layer j writes row j at column score_col[m] + t. The layers
+ * of one call share one rotary table, KV dtype and rotary style. Same bytes
+ * as rerotate_scatter_pages on the expanded plan. */
+DARIC_API int daric_copier_load_chunks(daric_copier* copier, int64_t num_layers, const char* const* layer_names,
+                                       int64_t layer_begin, int64_t layer_end, int64_t num_chunks,
+                                       const int64_t* chunk_stg_off, const int64_t* chunk_blk_off,
+                                       const int64_t* chunk_pages, const int32_t* block_ids,
+                                       int64_t block_ids_numel, int block_ids_device, int mode,
+                                       const int64_t* pos_a, const int64_t* pos_b, const int64_t* len,
+                                       float* scores, int64_t score_ld, const int64_t* score_col, void* stream);
+
 /* In-place re-rotation of K in paged caches, all layers in one launch.
  * Replaces the per-layer `_launch_triton_rerotate` / `_fused_rerotate_kernel`
  * loop (adapter.py:174-194, 268-295, 297-396). Work is given per segment

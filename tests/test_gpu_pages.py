@@ -7,7 +7,7 @@ import torch
 
 from daric_b200 import _lib
 from daric_b200.cache_ops import CacheCopier
-from daric_b200.reuse import build_load_plan, layer_block_bytes
+from daric_b200.reuse import build_chunk_plan, build_load_plan, layer_block_bytes
 from daric_b200.topo import CacheTopo
 from gpu_util import (layout_shape, oracle_layer, random_values, table_tensor, unique_blocks, bytes_np,
                       RAW_NP)
@@ -149,7 +149,10 @@ def test_out_of_range_block_is_skipped_and_flagged():
 
 
 # ------------------------------------------------------------------ fused --
-def _fused_case(layout, dt, tab_dt, neox, rot_dim, mode, H=2, D=128, bs=16, seed=0, scores=True):
+def _fused_case(layout, dt, tab_dt, neox, rot_dim, mode, H=2, D=128, bs=16, seed=0, scores=True, api="jobs"):
+    """api: "jobs" (rerotate_scatter_pages on the reference's per-job plan),
+    "chunks" (load_chunks, one descriptor per chunk) or "chunks-layerwise"
+    (load_chunks one layer range at a time)."""
     g, layers, topo, pf = _setup(layout, dt, nb=40, bs=bs, H=H, D=D, seed=seed)
     rng = np.random.default_rng(seed)
     lens = [32, 40, 16, 48, 5]          # partial pages in chunks 1 and 4
@@ -199,9 +202,17 @@ def _fused_case(layout, dt, tab_dt, neox, rot_dim, mode, H=2, D=128, bs=16, seed
         dev = R.rotate_tokens(ol[name][1], rot, gidx, c, s)
         exp_scores[li, col[m] + t] = dev
     sc = torch.full((len(layers), T), -1.0, device="cuda") if scores else None
-    kw = dict(scores=sc, job_score_row=plan.job_layer, meta_score_col=col) if scores else {}
-    copier.rerotate_scatter_pages(plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat,
-                                  plan.indices_offsets, plan.job_meta, mode, pos_a, pos_b, lens, **kw)
+    if api == "jobs":
+        kw = dict(scores=sc, job_score_row=plan.job_layer, meta_score_col=col) if scores else {}
+        copier.rerotate_scatter_pages(plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat,
+                                      plan.indices_offsets, plan.job_meta, mode, pos_a, pos_b, lens, **kw)
+    else:
+        cp = build_chunk_plan(topo, bpb, [(b,) for b in blocks], "cuda", base_offset=32)
+        L = len(cp.layer_names)
+        ranges = [(0, L)] if api == "chunks" else [(j, j + 1) for j in range(L)]
+        for rg in ranges:
+            copier.load_chunks(cp.c_names, cp.chunk_offsets, cp.chunk_blk_off, cp.chunk_pages, cp.block_ids, mode,
+                               pos_a, pos_b, lens, scores=sc, score_col=col if scores else None, layer_range=rg)
     torch.cuda.synchronize()
     assert _lib.device_errors(0) == 0
     for n, t in layers.items():
@@ -238,3 +249,149 @@ def test_fused_head_shapes(H, D, bs, page_kernel):
 
 def test_fused_without_scores():
     _fused_case("5d", "bf16", "bf16", True, 128, "flexible", scores=False)
+
+
+@pytest.mark.parametrize("api", ["chunks", "chunks-layerwise"])
+@pytest.mark.parametrize("mode", ["flexible", "delta"])
+@pytest.mark.parametrize("layout", ["5d", "5dpf", "4d", "3d"])
+def test_chunk_level_load_matches_oracle(layout, mode, api, page_kernel):
+    _fused_case(layout, "bf16", "bf16", True, 128, mode, api=api)
+
+
+@pytest.mark.parametrize("dt,tab", [("f16", "f16"), ("fp8", "bf16"), ("bf16", "f32")])
+def test_chunk_level_load_dtypes(dt, tab):
+    _fused_case("5d", dt, tab, True, 128, "flexible", api="chunks")
+    _fused_case("5d", dt, tab, False, 64, "delta", api="chunks-layerwise", seed=2)
+
+
+@pytest.mark.parametrize("H,D,bs", [(8, 128, 16), (1, 64, 16), (4, 128, 32)])
+def test_chunk_level_load_head_shapes(H, D, bs):
+    _fused_case("5d", "bf16", "bf16", True, D, "flexible", H=H, D=D, bs=bs, seed=H + D, api="chunks")
+
+
+def test_chunk_level_plain_scatter_matches_scatter_pages():
+    g, layers, topo, pf = _setup("5d", "bf16", nb=40, nlayers=3)
+    rng = np.random.default_rng(1)
+    blocks = unique_blocks(rng, 40, [3, 5, 2], with_null=True)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    plan = build_load_plan(topo, bpb, [(b,) for b in blocks], "cuda", base_offset=16)
+    cp = build_chunk_plan(topo, bpb, [(b,) for b in blocks], "cuda", base_offset=16)
+    store = random_values(((plan.total_bytes + 64) // 2,), "bf16", g, outliers=False).view(torch.uint8).reshape(-1)
+    a = {n: t.clone() for n, t in layers.items()}
+    ca, cb = CacheCopier(), CacheCopier()
+    for n in layers:
+        ca.register_layer(n, a[n], pf)
+        cb.register_layer(n, layers[n], pf)
+    ca.register_store(store)
+    cb.register_store(store)
+    ca.scatter_pages(plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat, plan.indices_offsets)
+    cb.load_chunks(cp.c_names, cp.chunk_offsets, cp.chunk_blk_off, cp.chunk_pages, cp.block_ids, "none")
+    torch.cuda.synchronize()
+    for n in layers:
+        assert torch.equal(a[n].view(torch.int16), layers[n].view(torch.int16)), n
+
+
+def test_chunk_level_load_argument_errors():
+    g, layers, topo, pf = _setup("5d", "bf16", nb=8, nlayers=2)
+    copier = CacheCopier()
+    for n, t in layers.items():
+        copier.register_layer(n, t, pf)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    cp = build_chunk_plan(topo, bpb, [([1, 2],)], "cuda")
+    copier.register_store(torch.zeros(cp.total_bytes - 16, dtype=torch.uint8, device="cuda"))
+    with pytest.raises(_lib.DaricError, match="store range out of bounds"):
+        copier.load_chunks(cp.c_names, cp.chunk_offsets, cp.chunk_blk_off, cp.chunk_pages, cp.block_ids, "none")
+    copier.register_store(torch.zeros(cp.total_bytes, dtype=torch.uint8, device="cuda"))
+    with pytest.raises(_lib.DaricError, match="reaches past block_ids"):
+        copier.load_chunks(cp.c_names, cp.chunk_offsets, [1], cp.chunk_pages, cp.block_ids, "none")
+    with pytest.raises(_lib.DaricError, match="register_rotary"):
+        copier.load_chunks(cp.c_names, cp.chunk_offsets, cp.chunk_blk_off, cp.chunk_pages, cp.block_ids,
+                           "flexible", [0], [5], [32])
+    with pytest.raises(_lib.DaricError, match="layer range"):
+        copier.load_chunks(cp.c_names, cp.chunk_offsets, cp.chunk_blk_off, cp.chunk_pages, cp.block_ids, "none",
+                           layer_range=(1, 3))
+
+
+@pytest.mark.parametrize("step", [1, 2, 5])
+def test_layerwise_load_from_host_matches_whole_load(step):
+    """load_layerwise (host -> staging per layer step on a copy stream,
+    overlapped with the fused kernel of the previous step) writes the same
+    paged KV and scores as one whole load of a staged chunk plan."""
+    from daric_b200.reuse import ReusedKVLoader
+    g, layers, topo, pf = _setup("5d", "bf16", nb=48, nlayers=5, seed=7)
+    rng = np.random.default_rng(7)
+    lens = [32, 40, 16, 48]
+    blocks = unique_blocks(rng, 48, [(n + 15) // 16 for n in lens])
+    table, _ = table_tensor(700, 128, 5e5, "bf16")
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    chunks = [(b,) for b in blocks]
+    total = sum(len(b) for b in blocks) * sum(bpb.values())
+    host = random_values((total // 2,), "bf16", g, outliers=False).view(torch.uint8).reshape(-1).cpu().pin_memory()
+    staging = torch.zeros(total, dtype=torch.uint8, device="cuda")
+    kv_a = {n: t.clone() for n, t in layers.items()}
+    rot = {n: (table, 128, True) for n in layers}
+    la = ReusedKVLoader(kv_a, topo, staging, rot)
+    lb = ReusedKVLoader(layers, topo, staging, rot)
+    pos = dict(mode="flexible", pos_a=[0, 300, 17, 600], pos_b=[40, 72, 112, 128], chunk_len=lens)
+    col = np.concatenate([[0], np.cumsum(lens)[:-1]]).tolist()
+    sa = torch.full((5, sum(lens)), -1.0, device="cuda")
+    sb = sa.clone()
+    cp = la.plan_chunks(chunks)
+    staging.copy_(host)
+    la.load_chunks(cp, scores=sa, score_col=col, **pos)
+    torch.cuda.synchronize()
+    staging.zero_()
+    lw = lb.load_layerwise(lb.plan_chunks(chunks), host, layers_per_step=step, scores=sb, score_col=col, **pos)
+    for j in range(5):
+        lw.wait_layer(j)
+    torch.cuda.synchronize()
+    assert _lib.device_errors(0) == 0
+    for n in layers:
+        assert torch.equal(kv_a[n].view(torch.int16), layers[n].view(torch.int16)), n
+    assert torch.equal(sa, sb)
+    with pytest.raises(IndexError):
+        lw.wait_layer(5)
+
+
+def test_fused_load_sees_a_table_written_just_before_registration():
+    """The factor pre-pass runs on a side stream; after a rotary table is
+    (re)registered it first waits for the caller's stream, so a table that
+    is still being written there (queued behind a long kernel) is read only
+    once written."""
+    g, layers, topo, pf = _setup("5d", "bf16", nb=24, nlayers=2, seed=5)
+    rng = np.random.default_rng(5)
+    blocks = unique_blocks(rng, 24, [2, 3])
+    lens = [32, 48]
+    copier = CacheCopier()
+    t1, raw1 = table_tensor(600, 128, 5e5, "bf16")
+    _, raw2 = table_tensor(600, 128, 1e4, "bf16")
+    for n, t in layers.items():
+        copier.register_layer(n, t, pf)
+        copier.register_rotary(n, t1, 128, True)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    plan = build_load_plan(topo, bpb, [(b,) for b in blocks], "cuda")
+    store = random_values(((plan.total_bytes + 64) // 2,), "bf16", g, outliers=False).view(torch.uint8).reshape(-1)
+    copier.register_store(store)
+    args = (plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat, plan.indices_offsets, plan.job_meta,
+            "flexible", [3, 100], [50, 7], lens)
+    copier.rerotate_scatter_pages(*args)
+    torch.cuda.synchronize()
+    ol = {n: oracle_layer(t, "bf16", pf) for n, t in layers.items()}  # before the second load
+    t2 = torch.zeros_like(t1)
+    src = torch.from_numpy(raw2.view(np.int16)).view(torch.bfloat16).pin_memory()
+    if hasattr(torch.cuda, "_sleep"):
+        torch.cuda._sleep(20_000_000)  # ~10 ms of GPU time queued before the table is written
+    t2.copy_(src, non_blocking=True)
+    for n in layers:
+        copier.register_rotary(n, t2, 128, True)
+    copier.rerotate_scatter_pages(*args)
+    P.scatter_pages({n: v[0] for n, v in ol.items()}, bytes_np(store), plan.layer_names, plan.offsets,
+                    plan.byte_sizes, plan.indices_flat.cpu().numpy(), plan.indices_offsets)
+    rot = R.Rotary(raw2.reshape(600, 128), "bf16", 128, True)
+    for j, (name, m) in enumerate(zip(plan.layer_names, plan.job_meta)):
+        t = np.arange(lens[m])
+        c, s = R.flexible_factors(rot, [3, 100][m] + t, [50, 7][m] + t)
+        R.rotate_tokens(ol[name][1], rot, R.gather_index(blocks[m], 16, 0, lens[m]), c, s)
+    torch.cuda.synchronize()
+    for n, t in layers.items():
+        np.testing.assert_array_equal(bytes_np(t).view(np.uint16), ol[n][0].mem.view(np.uint16))

@@ -62,3 +62,30 @@ def test_torch_cpu_baseline_matches_oracle():
     for i in range(L):
         got = kv[i].view(torch.int16).numpy().view(np.uint16).reshape(-1)
         np.testing.assert_array_equal(got, mems[f"l{i}"].view(np.uint16))
+
+
+def test_chunk_plan_covers_the_load_plan_jobs():
+    """The chunk plan (one descriptor per chunk) describes the same store
+    bytes as the per-(chunk, layer) job plan of the reference's copy plan,
+    and its layer ranges are contiguous slices of each chunk."""
+    from daric_b200.reuse import build_chunk_plan
+    names = [f"model.layers.{i}.attn" for i in range(11)]
+    topo = CacheTopo.single_group(names, 16, 2048, False)
+    bpb = {n: 2048 + 512 * (i % 3) for i, n in enumerate(sorted(names))}
+    chunks = [([5, 6, 7],), ([8],), ([],), ([10, 11, 12, 13],)]
+    lp = build_load_plan(topo, bpb, chunks, "cpu", base_offset=64)
+    cp = build_chunk_plan(topo, bpb, chunks, "cpu", base_offset=64)
+    L = len(names)
+    assert cp.layer_names == lp.layer_names[:L]
+    np.testing.assert_array_equal(cp.chunk_offsets, lp.chunk_offsets)
+    np.testing.assert_array_equal(cp.chunk_sizes, lp.chunk_sizes)
+    assert cp.block_ids.tolist() == [5, 6, 7, 8, 10, 11, 12, 13]
+    for m in range(len(chunks)):
+        for j in range(L):
+            off, size = cp.layer_regions(j, j + 1)
+            assert (off[m], size[m]) == (lp.offsets[m * L + j], lp.byte_sizes[m * L + j])
+            ids = lp.indices_flat[lp.indices_offsets[m * L + j]:lp.indices_offsets[m * L + j + 1]].tolist()
+            b0 = int(cp.chunk_blk_off[m])
+            assert ids == cp.block_ids[b0:b0 + int(cp.chunk_pages[m])].tolist()
+        off, size = cp.layer_regions(2, 7)
+        assert off[m] == lp.offsets[m * L + 2] and size[m] == sum(lp.byte_sizes[m * L + 2:m * L + 7])
