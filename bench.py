@@ -875,6 +875,48 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile_case(args):
+    """--profile-case: the small cases the ncu summaries under profiles/ were
+    captured on (no timing). The workload of --config with --layers layers
+    (inputs still larger than L2), then three calls of one path:
+      fused   : the fused re-rotate + scatter load (chunk-level entry point)
+      jobs    : the same through the reference-shaped job plan
+      strict  : in-place strict-PIC rotation of the request's middle groups
+      flexible: in-place flexible rotation of every chunk
+    """
+    from daric_b200 import _lib
+    if args.layers:
+        CONFIGS[args.config]["layers"] = args.layers
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = Workload(dev, seed=0, config=args.config, rank=0, world=args.tp_shard or 1)
+    from daric_b200.cache_ops import CacheCopier
+    copier = CacheCopier()
+    for n, t in wl.kv.items():
+        copier.register_layer(n, t, False)
+        copier.register_rotary(n, wl.table, wl.cfg["head_dim"], True)
+    req = [m for m in range(len(wl.chunk_len)) if wl.req_of[m] == 0]
+    req.sort(key=lambda m: wl.new_pos[m])
+    starts = np.concatenate([[0], np.cumsum([wl.chunk_len[m] for m in req])]).tolist()
+    for _ in range(3):
+        if args.profile_case == "fused":
+            wl.load()
+        elif args.profile_case == "jobs":
+            wl.load(api="jobs")
+        elif args.profile_case == "strict":
+            mid = range(1, len(req) - 1)
+            copier.rerotate_inplace(wl.names, "delta", wl.block_table, [0] * len(mid), [starts[i] for i in mid],
+                                    [wl.chunk_len[req[i]] for i in mid], [starts[i] for i in mid])
+        else:
+            copier.rerotate_inplace(wl.names, "flexible", wl.block_table, [0] * len(req),
+                                    [wl.new_pos[m] for m in req], [wl.chunk_len[m] for m in req],
+                                    [wl.old_pos[m] for m in req], [wl.new_pos[m] for m in req])
+    torch.cuda.synchronize()
+    assert _lib.device_errors(0) == 0
+    print(json.dumps({"profile_case": args.profile_case, "config": args.config, "layers": wl.cfg["layers"],
+                      "kv_heads": wl.heads, "algorithmic_bytes_fused": wl.bytes}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -892,6 +934,9 @@ def main():
                     help="run each step's selection in line after its load (default for input scores: on a "
                          "second stream, beside the next step's load)")
     ap.add_argument("--trace", action="store_true", help="add each timed step's load time (us) to the line")
+    ap.add_argument("--profile-case", choices=["fused", "jobs", "strict", "flexible"], default=None,
+                    help="build the workload and run one path three times, untimed (the ncu capture cases)")
+    ap.add_argument("--layers", type=int, default=0, help="with --profile-case: layers of the workload")
     ap.add_argument("--tp-shard", type=int, default=0,
                     help="config 4 on one GPU: run rank 0's KV-head shard of this TP degree (2/4/8)")
     args = ap.parse_args()
@@ -901,7 +946,9 @@ def main():
         CONFIGS[5]["hit"] = args.hit
     if args.recompute is not None:
         CONFIGS[args.config]["ratio"] = args.recompute
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
