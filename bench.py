@@ -181,13 +181,14 @@ class Workload:
         self.seg_len = list(self.req_tokens)
         self.seg_blk_off = self.req_blk_off.tolist()
 
-    def load(self, stream=0, api="chunks"):
+    def load(self, stream=0, api="chunks", scores=None):
         """The fused load of every chunk and layer: through the chunk-level
         entry point (one descriptor per chunk), or api="jobs" through the
-        reference-shaped per-(chunk, layer) job plan."""
+        reference-shaped per-(chunk, layer) job plan. Deviation configs write
+        their scores to ``scores`` (default: self.scores)."""
         kw = {}
         if self.cfg["scores"] == "deviation":
-            kw = dict(scores=self.scores, score_col=self.score_col)
+            kw = dict(scores=self.scores if scores is None else scores, score_col=self.score_col)
         if api == "jobs":
             self.loader.load(self.plan, mode="flexible", pos_a=self.old_pos, pos_b=self.new_pos,
                              chunk_len=self.chunk_len, stream=stream, **kw)
@@ -536,6 +537,31 @@ def run_tp(args, dist, rank, world, dev, stream, peak):
         allreduce_scores(wl.scores)
         wl.select()
     torch.cuda.synchronize()
+    # pipelined steps: the scores alternate between two buffers and each
+    # step's selection runs on a second stream beside the next step's load
+    bufs = [wl.scores, torch.empty_like(wl.scores)]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    sel_stream = torch.cuda.Stream(dev)
+    dist.barrier()
+    torch.cuda.synchronize()
+    preroll()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for i in range(steps):
+        b = i % 2
+        if i >= 2:
+            stream.wait_event(done[b])
+        wl.load(scores=bufs[b])
+        allreduce_scores(bufs[b])
+        sel_stream.wait_stream(stream)
+        with torch.cuda.stream(sel_stream):
+            wl.select(bufs[b])
+        done[b].record(sel_stream)
+    stream.wait_stream(sel_stream)
+    p1.record(stream)
+    torch.cuda.synchronize()
+    piped = p0.elapsed_time(p1) / steps
+    # in-line steps: load, all-reduce and selection timed one by one
     dist.barrier()
     torch.cuda.synchronize()
     preroll()
@@ -554,7 +580,7 @@ def run_tp(args, dist, rank, world, dev, stream, peak):
     sl = sum(x[2].elapsed_time(x[3]) for x in e) / steps
     step = e[0][0].elapsed_time(e[-1][3]) / steps
     load_min = min(x[0].elapsed_time(x[1]) for x in e)
-    load_m, ar_m, sl_m, step_m = _max_over_ranks([load, ar, sl, step], dist, dev)
+    load_m, ar_m, sl_m, step_m, piped_m = _max_over_ranks([load, ar, sl, step, piped], dist, dev)
     dist.barrier()
     # identical selection on every rank
     idx, slot, cnt = sel.idx.cpu().numpy(), sel.slot.cpu().numpy(), sel.count.cpu().numpy()
@@ -581,8 +607,10 @@ def run_tp(args, dist, rank, world, dev, stream, peak):
         tot = wl.bytes * world
         out = {
             "workload": "llama3-70b-32k-tp (BASELINE config 4)", "tp": world, "kv_heads_per_rank": wl.heads,
-            "steps": steps, "us_per_prompt": round(step_m * 1e3, 2),
-            "value_gbs": round(tot / (step_m * 1e-3) / 1e9, 1),
+            "steps": steps, "us_per_prompt": round(piped_m * 1e3, 2),
+            "value_gbs": round(tot / (piped_m * 1e-3) / 1e9, 1),
+            "pipelining": "selection of each step beside the next step's load (scores double-buffered)",
+            "us_per_prompt_in_line": round(step_m * 1e3, 2),
             "load_us": round(load_m * 1e3, 2), "load_us_min_rank0": round(load_min * 1e3, 2),
             "per_rank_load_frac": round(wl.bytes / (load_m * 1e-3) / 1e9 / peak, 4),
             "allreduce_us": round(ar_m * 1e3, 2), "allreduce_bytes": int(wl.scores.numel() * 4),
@@ -635,29 +663,37 @@ def run_ours(args):
     torch.cuda.synchronize()
     ev = _events(args.steps)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # With scores given as input (configs 2, 3, 5) a step's selection runs on
-    # a second stream after its load, beside the next step's load, as a
-    # pipelined server runs consecutive batches (--serial-select keeps it in
-    # line); scores produced by the load (config 4) keep it in line.
-    overlap = cfg["scores"] != "deviation" and not args.serial_select
+    # A step's selection runs on a second stream after its load, beside the
+    # next step's load, as a pipelined server runs consecutive batches
+    # (--serial-select keeps it in line). Scores produced by the load
+    # (config 4) alternate between two buffers, so the next load does not
+    # overwrite the scores a selection still reads.
+    overlap = not args.serial_select
+    deviation = cfg["scores"] == "deviation"
+    bufs = [wl.scores, torch.empty_like(wl.scores)] if (deviation and overlap) else [wl.scores]
+    sel_done = [torch.cuda.Event(), torch.cuda.Event()]
     sel_stream = torch.cuda.Stream(dev)
     with ClockSampler(local) as clk, NvmlSampler(dev) as nvml:
         preroll()
         start.record(stream)
         h0 = time.perf_counter()
         for i in range(args.steps):
+            b = i % len(bufs)
+            if len(bufs) > 1 and i >= 2:
+                stream.wait_event(sel_done[b])  # the selection of step i-2 has read buffer b
             ev[i][0].record(stream)
-            wl.load()
+            wl.load(scores=bufs[b])
             ev[i][1].record(stream)
             if tp:
                 from daric_b200.shard import allreduce_scores
-                allreduce_scores(wl.scores)
+                allreduce_scores(bufs[b])
             if overlap:
                 sel_stream.wait_stream(stream)
                 with torch.cuda.stream(sel_stream):
-                    wl.select()
+                    wl.select(bufs[b])
+                sel_done[b].record(sel_stream)
             else:
-                wl.select()
+                wl.select(bufs[b])
         host_us = (time.perf_counter() - h0) / args.steps * 1e6  # enqueue time per step
         stream.wait_stream(sel_stream)
         end.record(stream)

@@ -5,11 +5,13 @@
 
 #include <stdint.h>
 
+#include "internal.h"
+
 namespace daric {
 namespace bulk {
 
 constexpr int kMaxStages = 8;
-constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // a bounded wait gives up after 200 ms
+constexpr uint64_t kWaitNs = (uint64_t)kDefaultWaitNs;  // a bounded wait gives up after 200 ms
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -41,13 +43,16 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait for the phase with the given parity: false after kWaitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity: false after limit_ns
+// (kWaitNs unless a launch sets a shorter limit; below kWaitNs the clock is
+// read on every poll so that a short limit is honoured).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  const bool every = limit_ns < kWaitNs;
   for (uint32_t k = 1;; ++k) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((k & 63) == 0 && global_ns() - t0 > kWaitNs) return false;
+    if ((every || (k & 63) == 0) && global_ns() - t0 > limit_ns) return false;
   }
 }
 __device__ __forceinline__ void bulk_load(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {

@@ -1,18 +1,21 @@
 // Bulk-copy pipeline for the page copies of the reused-KV path (sm_100a).
 //
-// One persistent CTA per SM walks a contiguous range of units (one page of
-// one job). Each unit's regions (prefix_size x suffix bytes: the K and V
-// planes of a page) are moved by the copy engine with untiled
-// cp.async.bulk loads into a shared-memory stage (mbarrier completion,
-// NSTAGE stages in flight), the K rows are re-rotated in shared memory by
-// the consumer warps, and the whole page goes back out with cp.async.bulk
-// stores issued by a producer warp.
-// V bytes never pass through registers. Same byte mapping, block-0 skip,
-// rotation math and deviation scores as the SIMT kernels in page_kernels.cu.
+// Persistent CTAs (one, two or four per SM) each walk a contiguous range of
+// units (up to 8 consecutive pages of one job). Each unit's regions
+// (prefix_size x suffix bytes per page: the K and V planes) are moved by the
+// SM's copy unit with untiled cp.async.bulk loads into a shared-memory stage
+// (mbarrier completion, NSTAGE stages in flight), the K rows are re-rotated
+// in shared memory by the consumer warps, and the unit goes back out with
+// cp.async.bulk stores issued by a producer warp. V bytes never pass
+// through registers. Same byte mapping, block-0 skip, rotation math and
+// deviation scores as the SIMT kernels in page_kernels.cu. Jobs come from a
+// job table, or (chunk-level loads) are derived from one descriptor per
+// chunk.
 //
-// Every wait is bounded: an mbarrier wait that exceeds kWaitNs (200 ms)
-// sets DEV_ERR_TIMEOUT, drains the copies this CTA has in flight (again with
-// a bound) and returns.
+// Every wait is bounded: an mbarrier wait that exceeds its limit (200 ms
+// unless the launch sets a shorter one) sets DEV_ERR_TIMEOUT, the producer
+// drains the copies this CTA has in flight (with the 200 ms bound) and the
+// CTA returns.
 #include <map>
 #include <mutex>
 
@@ -366,6 +369,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     // loads of unit i into stage i % NS (warp-synchronous: every lane calls);
     // false when a wait timed out
     auto issue = [&](int64_t i) -> bool {
+      if (g.unarmed && i == 0) return true;  // test only: nothing arms unit 0
       const int64_t b = i / 32;
       if (b != batch) {
         prefetch(b);
@@ -387,7 +391,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
           // units up to x may still read the buffer's old block: wait for
           // each of them (consumer groups release units out of order)
           for (int64_t y = waited + 1; y <= x; ++y) {
-            const bool ok = mbar_wait(&empty[y % NS], (uint32_t)((y / NS) & 1));
+            const bool ok = mbar_wait(&empty[y % NS], (uint32_t)((y / NS) & 1), (uint64_t)g.wait_ns);
             if (__any_sync(FULL, !ok)) return false;
           }
           if (f) fkey1 = fkey; else fkey0 = fkey;
@@ -461,7 +465,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     int64_t i = 0;
     for (; ok && i < n; ++i) {
       const int s = (int)(i % NS);
-      const bool got = mbar_wait(&empty[s], (uint32_t)((i / NS) & 1));
+      const bool got = mbar_wait(&empty[s], (uint32_t)((i / NS) & 1), (uint64_t)g.wait_ns);
       if (__any_sync(FULL, !got)) {
         ok = false;
         break;
@@ -530,7 +534,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       atomicOr(p.err, DEV_ERR_TIMEOUT);
       // drain the loads that may still be in flight into this CTA's stages
       // (units not yet released by the consumers)
-      for (int64_t k = i; k < issued; ++k) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
+      for (int64_t k = i; k < issued; ++k)
+        if (!(g.unarmed && k == 0)) mbar_wait(&full[k % NS], (uint32_t)((k / NS) & 1));
     }
     bulk_wait_all();
     return;
@@ -542,7 +547,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   const bool cst = !GATHER && g.cstore;
   for (int64_t i = grp; i < n; i += CG) {
     const int s = (int)(i % NS);
-    if (!mbar_wait(&full[s], (uint32_t)((i / NS) & 1))) {
+    if (!mbar_wait(&full[s], (uint32_t)((i / NS) & 1), (uint64_t)g.wait_ns)) {
       atomicOr(p.err, DEV_ERR_TIMEOUT);
       break;
     }

@@ -539,6 +539,21 @@ JobPlan plan_jobs(daric_copier* c, int64_t num_jobs, const char* const* names, c
   return jp;
 }
 
+// Limit of the pipelines' waits: DARIC_WAIT_NS (1 ns .. 200 ms) when set,
+// else 200 ms. Tests make a wait run out with a short limit together with
+// DARIC_TEST_UNARMED=1, which leaves each CTA's first unit unarmed (a
+// barrier nothing completes): the call returns and reports the time-out.
+int32_t pipeline_wait_ns() {
+  const char* v = std::getenv("DARIC_WAIT_NS");
+  if (!v) return kDefaultWaitNs;
+  const long x = std::strtol(v, nullptr, 10);
+  return (x >= 1 && x <= kDefaultWaitNs) ? (int32_t)x : kDefaultWaitNs;
+}
+int32_t pipeline_unarmed() {
+  const char* v = std::getenv("DARIC_TEST_UNARMED");
+  return (v && std::strcmp(v, "1") == 0) ? 1 : 0;
+}
+
 // Page-kernel choice: the bulk-copy pipeline unless DARIC_PAGE_KERNEL=simt
 // (diagnostic switch for A/B measurements of the two implementations).
 bool bulk_pipeline_enabled() {
@@ -643,6 +658,8 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
       cw -= cw % (int)groups;
       g.cwarps = cw > 0 ? cw : (int)groups;
       g.cstore = cstore ? 1 : 0;
+      g.wait_ns = pipeline_wait_ns();
+      g.unarmed = pipeline_unarmed();
       return true;
     };
     // The largest unit (up to the per-CTA target) that fits three stages,
@@ -701,6 +718,8 @@ InplaceGeom plan_inplace(const DeviceCtx& dc, const std::vector<LayerDev>& layer
       g.ctas_per_sm = ctas;
       g.cwarps = cwarps;
       g.tab_dtype = tab_dtype;
+      g.wait_ns = pipeline_wait_ns();
+      g.unarmed = pipeline_unarmed();
       return g;
     }
     if (pin) break;

@@ -1,8 +1,9 @@
 // Internal definitions shared by the host side (capi.cpp) and the kernels.
 //
 // Device descriptors are uploaded once per call as one contiguous blob
-// (launch header, layer table, job table, chunk table) through a pinned ring
-// (desc_ring.cpp); kernels read them through __ldg-cached loads.
+// (layer table, job or chunk table, factor runs, unit groups) through a
+// pinned ring (capi.cpp, class Upload); kernels read them through
+// read-only-cached loads.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -199,6 +200,8 @@ struct InplaceGeom {
   int32_t ctas_per_sm;
   int32_t cwarps;       // consumer warps per CTA (plus one producer warp)
   int32_t tab_dtype;    // rotary table dtype (factors are read from the table)
+  int32_t wait_ns;      // limit of a pipeline wait (ns); the drain after a time-out keeps 200 ms
+  int32_t unarmed;      // test only: each CTA's first unit is never armed, so its waits run out
   int32_t pad;
 };
 
@@ -300,8 +303,15 @@ struct BulkGeom {
   int32_t cgroups;      // consumer-warp groups (1, 2 or 4) taking alternate units
   int32_t cwarps;       // consumer warps per CTA (plus one producer warp)
   int32_t cstore;       // scatter: consumer warps write the paged cache (no bulk stores)
+  int32_t wait_ns;      // limit of a pipeline wait (ns); the drain after a time-out keeps 200 ms
+  int32_t unarmed;      // test only: each CTA's first unit is never armed, so its waits run out
   int32_t pad;
 };
+
+// Limit of one bounded wait in the pipelined kernels (ns). DARIC_WAIT_NS
+// sets a shorter limit for the waits of a launch (tests make a wait run out
+// with it); the drain of in-flight copies after a time-out keeps this one.
+constexpr int32_t kDefaultWaitNs = 200 * 1000 * 1000;
 
 // Bytes of the bulk pipeline's shared-memory header (barriers + stage meta).
 constexpr int kBulkHeader = 2048;

@@ -395,3 +395,36 @@ def test_fused_load_sees_a_table_written_just_before_registration():
     torch.cuda.synchronize()
     for n, t in layers.items():
         np.testing.assert_array_equal(bytes_np(t).view(np.uint16), ol[n][0].mem.view(np.uint16))
+
+
+def test_pipeline_wait_time_out_reports_and_leaves_the_device_usable(monkeypatch):
+    """With each CTA's first unit left unarmed (a barrier nothing completes,
+    DARIC_TEST_UNARMED) and a 2 ms wait limit (DARIC_WAIT_NS), the pipelines'
+    waits run out: the calls return, daric_device_errors reports bit 8, and
+    the next calls produce the oracle's bytes (the kernels drain their copies
+    in flight before returning; nothing faults)."""
+    g, layers, topo, pf = _setup("5d", "bf16", nb=40, nlayers=2, seed=9)
+    rng = np.random.default_rng(9)
+    blocks = unique_blocks(rng, 40, [3, 4])
+    table, _ = table_tensor(600, 128, 5e5, "bf16")
+    copier = CacheCopier()
+    for n, t in layers.items():
+        copier.register_layer(n, t, pf)
+        copier.register_rotary(n, table, 128, True)
+    bpb = {n: layer_block_bytes(t, pf) for n, t in layers.items()}
+    plan = build_load_plan(topo, bpb, [(b,) for b in blocks], "cuda")
+    store = random_values(((plan.total_bytes + 64) // 2,), "bf16", g, outliers=False).view(torch.uint8).reshape(-1)
+    copier.register_store(store)
+    bt = torch.tensor(blocks[0] + blocks[1], dtype=torch.int32, device="cuda")
+    assert _lib.device_errors(0) == 0
+    monkeypatch.setenv("DARIC_WAIT_NS", "2000000")
+    monkeypatch.setenv("DARIC_TEST_UNARMED", "1")
+    copier.rerotate_scatter_pages(plan.layer_names, plan.offsets, plan.byte_sizes, plan.indices_flat,
+                                  plan.indices_offsets, plan.job_meta, "flexible", [3, 100], [50, 7], [48, 64])
+    assert _lib.device_errors(0) == 8
+    copier.rerotate_inplace(list(layers), "delta", bt, [0, 3], [0, 0], [48, 64], [17, 29])
+    assert _lib.device_errors(0) == 8
+    monkeypatch.delenv("DARIC_WAIT_NS")
+    monkeypatch.delenv("DARIC_TEST_UNARMED")
+    _fused_case("5d", "bf16", "bf16", True, 128, "flexible", seed=9)
+    _fused_case("5d", "bf16", "bf16", True, 128, "delta", seed=10, api="chunks")
