@@ -24,6 +24,17 @@ from ..select import ptrs_to_slots
 from ..topo import CacheTopo
 from .policy import DARICPolicy
 
+
+def _policy_class():
+    """The recompute policy: DARIC's own DARICPolicy when this runs inside a
+    DARIC installation (the scheduler logic stays the reference's), else the
+    bit-exact restatement in daric_b200.adaption.policy."""
+    try:
+        from daric.adaption.policy import DARICPolicy as reference_policy  # type: ignore
+        return reference_policy
+    except Exception:
+        return DARICPolicy
+
 __all__ = ["Adapter", "AdaptionConfig"]
 
 
@@ -66,7 +77,8 @@ class Adapter:
         self.kvcaches: dict[str, torch.Tensor] = {}
         self.rotary_embeds: dict[str, object] = {}
         if config.recompute_policy == "daric":
-            self.recompute_policy = DARICPolicy(config.recompute_avg_num, function=config.function, r=config.r)
+            self.recompute_policy = _policy_class()(config.recompute_avg_num, function=config.function,
+                                                     r=config.r)
         else:
             self.recompute_policy = None
         self.rerotate = config.rerotate
