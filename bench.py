@@ -919,6 +919,7 @@ def run_profile_case(args):
       jobs    : the same through the reference-shaped job plan
       strict  : in-place strict-PIC rotation of the request's middle groups
       flexible: in-place flexible rotation of every chunk
+      select  : the top-k selection of every layer on lognormal scores
     """
     from daric_b200 import _lib
     if args.layers:
@@ -934,8 +935,13 @@ def run_profile_case(args):
     req = [m for m in range(len(wl.chunk_len)) if wl.req_of[m] == 0]
     req.sort(key=lambda m: wl.new_pos[m])
     starts = np.concatenate([[0], np.cumsum([wl.chunk_len[m] for m in req])]).tolist()
+    if args.profile_case == "select":
+        torch.manual_seed(1)
+        wl.scores.copy_(torch.distributions.LogNormal(0.0, 1.0).sample(tuple(wl.scores.shape)))
     for _ in range(3):
-        if args.profile_case == "fused":
+        if args.profile_case == "select":
+            wl.select()
+        elif args.profile_case == "fused":
             wl.load()
         elif args.profile_case == "jobs":
             wl.load(api="jobs")
@@ -970,7 +976,7 @@ def main():
                     help="run each step's selection in line after its load (default for input scores: on a "
                          "second stream, beside the next step's load)")
     ap.add_argument("--trace", action="store_true", help="add each timed step's load time (us) to the line")
-    ap.add_argument("--profile-case", choices=["fused", "jobs", "strict", "flexible"], default=None,
+    ap.add_argument("--profile-case", choices=["fused", "jobs", "strict", "flexible", "select"], default=None,
                     help="build the workload and run one path three times, untimed (the ncu capture cases)")
     ap.add_argument("--layers", type=int, default=0, help="with --profile-case: layers of the workload")
     ap.add_argument("--tp-shard", type=int, default=0,
