@@ -573,7 +573,7 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // the units reading the previous block are done), else the consumer warps
 // read it from L2.
 // Small pages run 2 or 4 CTAs per SM (more with deviation scores), others
-// one (DARIC_BULK_CTAS pins 1, 2 or 4; each CTA has its own producer warp and
+// one (DARIC_BULK_CTAS pins 1 to 4; each CTA has its own producer warp and
 // a share of the consumer warps and shared memory);
 // DARIC_BULK_CGROUPS splits the consumer warps into 2 or 4 groups.
 // DARIC_BULK_CTAS, DARIC_BULK_CGROUPS, DARIC_BULK_CWARPS,
@@ -619,7 +619,7 @@ BulkGeom plan_bulk(const DeviceCtx& dc, const std::vector<LayerDev>& layers, boo
   int ctas = 1;
   if (page <= 8 * 1024) ctas = scores ? 4 : 2;
   else if (page <= 16 * 1024 && scores) ctas = 2;
-  if (pin_ctas == 1 || pin_ctas == 2 || pin_ctas == 4) ctas = (int)pin_ctas;
+  if (pin_ctas >= 1 && pin_ctas <= 4) ctas = (int)pin_ctas;
   for (; ctas >= 1; ctas /= 2) {
     const size_t budget =
         std::min<size_t>((size_t)dc.smem_optin, (size_t)dc.smem_sm / (size_t)ctas - 1024);  // 1 KiB reserved per CTA

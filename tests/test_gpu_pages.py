@@ -312,8 +312,8 @@ def test_chunk_level_load_argument_errors():
                            layer_range=(1, 3))
 
 
-@pytest.mark.parametrize("step", [1, 2, 5])
-def test_layerwise_load_from_host_matches_whole_load(step):
+@pytest.mark.parametrize("step,gap", [(1, 0), (2, 4096), (5, 0)])
+def test_layerwise_load_from_host_matches_whole_load(step, gap):
     """load_layerwise (host -> staging per layer step on a copy stream,
     overlapped with the fused kernel of the previous step) writes the same
     paged KV and scores as one whole load of a staged chunk plan."""
@@ -341,7 +341,15 @@ def test_layerwise_load_from_host_matches_whole_load(step):
     la.load_chunks(cp, scores=sa, score_col=col, **pos)
     torch.cuda.synchronize()
     staging.zero_()
-    lw = lb.load_layerwise(lb.plan_chunks(chunks), host, layers_per_step=step, scores=sb, score_col=col, **pos)
+    # the store keeps its chunks elsewhere in its shared memory: each chunk
+    # `gap` bytes further than the one before (host_offsets)
+    host_off = cp.chunk_offsets + gap * (1 + np.arange(len(chunks)))
+    shm = torch.zeros(total + gap * (len(chunks) + 1), dtype=torch.uint8).pin_memory()
+    for m in range(len(chunks)):
+        o, n = int(cp.chunk_offsets[m]), int(cp.chunk_sizes[m])
+        shm[int(host_off[m]):int(host_off[m]) + n] = host[o:o + n]
+    lw = lb.load_layerwise(lb.plan_chunks(chunks), shm, host_offsets=host_off, layers_per_step=step, scores=sb,
+                           score_col=col, **pos)
     for j in range(5):
         lw.wait_layer(j)
     torch.cuda.synchronize()
