@@ -1,7 +1,10 @@
 // Bulk-copy pipeline for the page copies of the reused-KV path (sm_100a).
 //
-// Persistent CTAs (one, two or four per SM) each walk a contiguous range of
-// units (up to 8 consecutive pages of one job). Each unit's regions
+// Persistent CTAs (one to four per SM) each walk batches of consecutive
+// units (up to 8 consecutive pages of one job): a first batch by CTA index,
+// then batches claimed from the launch's work counter, smaller towards the
+// end, so CTAs that start late (an SM busy with another stream's kernel)
+// take fewer units instead of finishing late. Each unit's regions
 // (prefix_size x suffix bytes per page: the K and V planes) are moved by the
 // SM's copy unit with untiled cp.async.bulk loads into a shared-memory stage
 // (mbarrier completion, NSTAGE stages in flight), the K rows are re-rotated
@@ -97,9 +100,14 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
                                                  int64_t len, float* tok_dev, int tid, int nthreads, bool cst) {
   constexpr int ES = FC ? 8 : 16;  // bytes per factor entry
   constexpr int NG = NEOX ? E::kPerVec / 2 : E::kPerVec / 4;  // factor entries per task
+  // the unit's layer and stage fields, read once into registers: every
+  // shared-memory store below is an asm statement with a memory clobber,
+  // after which a field read through L or st would be loaded again
   const int P = L.pair_vecs;
   const int bs = L.page_size;
   const int R = L.nrows / bs;  // rows of one token
+  const FastDiv pair_div = L.pair_div, tok_mod = L.tok_mod;
+  const int row_bytes = L.row_bytes, rbytes = st.rbytes, skipmask = st.skipmask;
   // token-major rows (one run): row = sl * R + k; head-major (4-D): k * bs + sl
   const bool tok_major = (int)L.tok_div.d == R;
   const int sl_mul = tok_major ? R : 1, k_mul = tok_major ? 1 : bs;
@@ -107,7 +115,7 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
   const int64_t tok_base = (int64_t)st.pl0 * bs;
   // plane-major stage: region pf of page g at (pf * pages_per_unit + g) * rbytes
-  const uint32_t base = smem_addr(stage) + (uint32_t)(L.k_prefix * pages_per_unit) * (uint32_t)st.rbytes;
+  const uint32_t base = smem_addr(stage) + (uint32_t)(L.k_prefix * pages_per_unit) * (uint32_t)rbytes;
   const int base_tasks = st.npg * bs * P;
   int hs = 1;
   while (hs < R && R % (2 * hs) == 0 && base_tasks * hs < nthreads && (!SCORE || P * hs * 2 <= 32)) hs *= 2;
@@ -121,14 +129,14 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
     int slot = -1;    // unit token of this lane's task
     bool rot = false;
     if (t < ntask) {
-      const int tc = (int)fdiv((uint32_t)t, L.pair_div);
+      const int tc = (int)fdiv((uint32_t)t, pair_div);
       const int c = t - tc * P;
       const int hq = tc & (hs - 1);
       const int gs = tc >> hshift;  // unit token g * bs + sl
-      const int g = (int)fdiv((uint32_t)gs, L.tok_mod);
+      const int g = (int)fdiv((uint32_t)gs, tok_mod);
       const int sl = gs - g * bs;
       slot = gs;
-      rot = !((st.skipmask >> g) & 1) && tok_base + gs < len;
+      rot = !((skipmask >> g) & 1) && tok_base + gs < len;
       if (rot) {
         float4 q[NG];
         const uint8_t* fq = fac_unit + (gs * per_tok + c) * ES;
@@ -147,7 +155,7 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
                       : __ldg(reinterpret_cast<const float4*>(gp));
           }
         }
-        const uint32_t cb = base + (uint32_t)(g * st.rbytes + c * 16);
+        const uint32_t cb = base + (uint32_t)(g * rbytes + c * 16);
         // consumer stores: the rotated vectors go straight to the page's K
         // region in the paged cache
         uint8_t* gb = cst ? st.base + (int64_t)L.k_prefix * st.prefix_stride + (int64_t)st.blk[g] * st.page_stride +
@@ -155,7 +163,7 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
                           : nullptr;
 #pragma unroll 2
         for (int k = hq; k < R; k += hs) {
-          const int roff = (sl * sl_mul + k * k_mul) * L.row_bytes;
+          const int roff = (sl * sl_mul + k * k_mul) * row_bytes;
           const uint32_t ad = cb + (uint32_t)roff;
           uint4 lo = lds128(ad), hi;
           if (NEOX) hi = lds128(ad + hi_off);
@@ -220,10 +228,12 @@ __device__ __forceinline__ void store_rest(const LayerDev* Lk, const StageMeta& 
 }
 
 // Warp-specialised pipeline. Warps 0..cwarps-1 rotate (in CG groups that
-// take alternate units); the last warp is the producer. Its 32 lanes prefetch the copy plans of 32 units at a time; for
-// unit u the lane that prefetched it writes the stage metadata and arms
-// full[u % NS], then the warp issues the unit's bulk loads (one region per
-// lane). When every consumer warp has released the unit (empty[s]) the warp
+// take alternate units); the last warp is the producer. Its lanes prefetch
+// the copy plans of one batch (up to 32 units) at a time; for the CTA's
+// unit i the lane that prefetched it writes the stage metadata and arms
+// full[i % NS], then the warp issues the unit's bulk loads (one region per
+// lane). When no batch is left the producer arms one end marker (npg = -1)
+// per consumer group instead of a unit. When every consumer warp has released the unit (empty[s]) the warp
 // issues its bulk stores (one region per lane) and reuses the stage of the
 // previous unit once those stores have read it.
 // Units run page range by page range across the jobs of a group, so
@@ -259,11 +269,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   const int CG = (g.cgroups > 1 && g.nstage % g.cgroups == 0) ? g.cgroups : 1;
   const int gwarps = cwarps / CG;
 
-  int64_t ubeg, uend;
-  cta_range(p.total_units, ubeg, uend);
-  if (ubeg >= uend) return;
-  const int64_t n = uend - ubeg;
-
   // Region pf of job-local page pl (block blk): store side at
   // stg_off + (pf * n_sel + pl) * rbytes, layer side at
   // base + pf * prefix_stride + blk * page_stride.
@@ -281,12 +286,37 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
 
   if (producer) {
     const unsigned FULL = 0xffffffffu;
-    int64_t gcur = find_group(p.groups, p.num_groups, ubeg);
-    int64_t batch = -1;
+    // the CTA's units: batch after batch, the current one is local units
+    // [bbeg, bend) = global units [u0, u0 + bend - bbeg); n = the CTA's unit
+    // count once a claim came back empty (-1 before)
+    int64_t bbeg = 0, bend = 0, u0 = 0, n = -1;
+    int nclaims = 0;
     StageMeta mine{};  // this lane's unit of the current batch
-    auto prefetch = [&](int64_t b) {  // all lanes
-      const int64_t i = b * 32 + lane;
-      int64_t gi = gcur;
+    // next batch: the first by CTA index, then from the work counter, about
+    // half the units left per CTA (1 to 32); returns its size (0: none left)
+    auto claim = [&]() -> int {  // all lanes
+      const uint64_t total = (uint64_t)p.total_units;
+      uint64_t start = 0;
+      int m = 0;
+      if (lane == 0) {
+        uint64_t want = (uint64_t)p.first_batch;
+        if (nclaims == 0) {
+          start = (uint64_t)blockIdx.x * want;
+        } else {
+          const uint64_t cur = *reinterpret_cast<volatile unsigned long long*>(p.work);
+          const uint64_t left = total > cur ? total - cur : 0;
+          want = left / (2 * (uint64_t)gridDim.x);
+          want = want < 1 ? 1 : (want > 32 ? 32 : want);
+          start = atomicAdd(p.work, (unsigned long long)want);
+        }
+        m = start < total ? (int)(total - start < want ? total - start : want) : 0;
+      }
+      ++nclaims;
+      u0 = (int64_t)__shfl_sync(FULL, (unsigned long long)start, 0);
+      return __shfl_sync(FULL, m, 0);
+    };
+    auto prefetch = [&](int m) {  // all lanes: lane < m prefetches unit u0 + lane
+      int64_t gi = find_group(p.groups, p.num_groups, u0);
       mine.npg = 0;
       mine.skipmask = 0;
       mine.sn = 0;
@@ -295,8 +325,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       mine.fac_bytes = 0;
       mine.fkey = -1;
       mine.len = 0;
-      if (i < n) {
-        const int64_t u = ubeg + i;
+      if (lane < m) {
+        const int64_t u = u0 + lane;
         while (gi + 1 < p.num_groups && p.groups[gi + 1].unit_begin <= u) ++gi;
         const GroupDev G = p.groups[gi];
         const int64_t local = u - G.unit_begin;
@@ -358,7 +388,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
           }
         }
       }
-      gcur = __shfl_sync(FULL, gi, 31);
     };
     // factor buffers: the block each holds and the last unit that reads it
     // (scalar pairs: no local-memory arrays)
@@ -370,13 +399,26 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     // false when a wait timed out
     auto issue = [&](int64_t i) -> bool {
       if (g.unarmed && i == 0) return true;  // test only: nothing arms unit 0
-      const int64_t b = i / 32;
-      if (b != batch) {
-        prefetch(b);
-        batch = b;
+      if (n < 0 && i >= bend) {
+        const int m = claim();
+        if (m == 0) {
+          n = i;
+        } else {
+          bbeg = i;
+          bend = i + m;
+          prefetch(m);
+        }
       }
-      const int k = (int)(i - b * 32);
       const int s = (int)(i % NS);
+      if (n >= 0 && i >= n) {  // end marker of consumer group (i - n)
+        if (lane == 0) {
+          meta[s].npg = -1;
+          mbar_arrive(&full[s]);
+        }
+        __syncwarp();
+        return true;
+      }
+      const int k = (int)(i - bbeg);
       const long long fkey = __shfl_sync(FULL, (long long)mine.fkey, k);
       const int npg = __shfl_sync(FULL, mine.npg, k);
       const int live = npg - __popc(__shfl_sync(FULL, mine.skipmask, k));
@@ -454,7 +496,9 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     // consumers release it (NS in flight)
     const bool cst = !GATHER && g.cstore;
     const int inflight = cst ? NS : NS - 1;
-    while (issued < inflight && issued < n) {
+    // units and end markers still to arm
+    auto more = [&]() { return n < 0 || issued < n + CG; };
+    while (issued < inflight && more()) {
       if (!issue(issued)) {
         ok = false;
         break;
@@ -463,7 +507,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
     }
     bool prev_stored = false;  // unit i-1 has a pending store group (every lane)
     int64_t i = 0;
-    for (; ok && i < n; ++i) {
+    for (; ok && (n < 0 || i < n); ++i) {
       const int s = (int)(i % NS);
       const bool got = mbar_wait(&empty[s], (uint32_t)((i / NS) & 1), (uint64_t)g.wait_ns);
       if (__any_sync(FULL, !got)) {
@@ -519,7 +563,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       // the next load goes into the stage of unit i-1 (bulk stores: they must
       // have read it; unit i's group, committed last, may still be pending)
       // or of unit i (consumer stores)
-      if (issued < n) {
+      if (more()) {
         if (prev_stored) {
           if (stored) bulk_wait_read<1>(); else bulk_wait_read<0>();
         }
@@ -529,6 +573,13 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
       }
       prev_stored = stored;
       __syncwarp();
+    }
+    // end markers the loop did not reach (consumer groups beyond the units in
+    // flight): they write only stage metadata, and every unit that used
+    // their stages has been released
+    while (ok && more()) {
+      issue(issued);
+      ++issued;
     }
     if (!ok && lane == 0) {
       atomicOr(p.err, DEV_ERR_TIMEOUT);
@@ -545,13 +596,14 @@ __global__ void __launch_bounds__(kBulkThreads, 1) bulk_pages_kernel(PageLaunch 
   const int grp = warp / gwarps;
   const int gtid = tid - grp * gwarps * 32;
   const bool cst = !GATHER && g.cstore;
-  for (int64_t i = grp; i < n; i += CG) {
+  for (int64_t i = grp;; i += CG) {
     const int s = (int)(i % NS);
     if (!mbar_wait(&full[s], (uint32_t)((i / NS) & 1), (uint64_t)g.wait_ns)) {
       atomicOr(p.err, DEV_ERR_TIMEOUT);
       break;
     }
     const StageMeta& st = meta[s];
+    if (st.npg < 0) break;  // end marker
     const bool live = st.npg > __popc(st.skipmask);
     uint8_t* stage = stages + (size_t)s * g.stage_bytes;
     const LayerDev* Lk = nullptr;
@@ -585,8 +637,9 @@ void launch_bulk(K kernel, const PageLaunch& p, const BulkGeom& g, int sm_count,
       cur = smem;
     }
   }
-  const int64_t ctas = (int64_t)sm_count * g.ctas_per_sm;
-  const int grid = (int)(p.total_units < ctas ? p.total_units : ctas);
+  const int grid = bulk_grid(p.total_units, sm_count, g.ctas_per_sm);
+  if (p.work == nullptr || p.first_batch != bulk_first_batch(p.total_units, grid))
+    throw Error(DARIC_ERR_INVALID, "internal: bulk launch without its work counter");
   const int threads = (g.cwarps + 1) * 32;
   kernel<<<grid, threads, smem, s>>>(p, g);
   DARIC_CUDA(cudaGetLastError());

@@ -322,6 +322,21 @@ struct Blob {
   }
 };
 
+// Work counter of a bulk-pipeline launch, written into its uploaded
+// descriptors: the units past every CTA's first batch. Returns the first
+// batch (0 when the launch does not run the bulk pipeline).
+int64_t put_work_counter(uint8_t* dst, int64_t units, const BulkGeom& bg, int sm_count) {
+  unsigned long long start = 0;
+  int64_t first = 0;
+  if (bg.nstage >= 3 && units > 0) {
+    const int grid = bulk_grid(units, sm_count, bg.ctas_per_sm);
+    first = bulk_first_batch(units, grid);
+    start = (unsigned long long)std::min<int64_t>(units, first * grid);
+  }
+  std::memcpy(dst, &start, sizeof(start));
+  return first;
+}
+
 // ----------------------------------------------------------- layers -----
 struct LayerHost {
   std::string name;
@@ -862,12 +877,14 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   const size_t o_metas = b.add(metas.size() * sizeof(MetaDev));
   const size_t o_runs = b.add(runs.size() * sizeof(FacJobDev));
   const size_t o_groups = b.add(groups.size() * sizeof(GroupDev));
+  const size_t o_work = b.add(sizeof(unsigned long long));
   Upload up(dc, b.size);
   std::memcpy(up.host() + o_layers, layers.data(), layers.size() * sizeof(LayerDev));
   std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
   if (!metas.empty()) std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
   if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
   if (!groups.empty()) std::memcpy(up.host() + o_groups, groups.data(), groups.size() * sizeof(GroupDev));
+  const int64_t first_batch = put_work_counter(up.host() + o_work, units, bg, dc.sm_count);
   std::unique_ptr<FactorPass> lease;
   if (fac_bytes > 0) lease = std::make_unique<FactorPass>(dc, (size_t)fac_bytes, stream);
   float4* fac = lease ? reinterpret_cast<float4*>(lease->ptr()) : nullptr;
@@ -902,6 +919,8 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
   p.fac = fac;
   p.groups = reinterpret_cast<const GroupDev*>(up.dev() + o_groups);
   p.num_groups = (int64_t)groups.size();
+  p.work = reinterpret_cast<unsigned long long*>(up.dev() + o_work);
+  p.first_batch = first_batch;
   if (bg.nstage >= 3) {
     if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
     else launch_bulk_plain(p, bg, gather, dc.sm_count, stream);
@@ -1098,12 +1117,14 @@ void run_chunk_load(daric_copier* c, int64_t num_layers, const char* const* name
   const size_t o_metas = b.add(metas.size() * sizeof(MetaDev));
   const size_t o_runs = b.add(runs.size() * sizeof(FacJobDev));
   const size_t o_groups = b.add(groups.size() * sizeof(GroupDev));
+  const size_t o_work = b.add(sizeof(unsigned long long));
   Upload up(dc, b.size);
   std::memcpy(up.host() + o_layers, layers.data(), layers.size() * sizeof(LayerDev));
   if (!jobs.empty()) std::memcpy(up.host() + o_jobs, jobs.data(), jobs.size() * sizeof(JobDev));
   std::memcpy(up.host() + o_metas, metas.data(), metas.size() * sizeof(MetaDev));
   if (!runs.empty()) std::memcpy(up.host() + o_runs, runs.data(), runs.size() * sizeof(FacJobDev));
   if (!groups.empty()) std::memcpy(up.host() + o_groups, groups.data(), groups.size() * sizeof(GroupDev));
+  const int64_t first_batch = put_work_counter(up.host() + o_work, units, bg, dc.sm_count);
   std::unique_ptr<FactorPass> lease;
   if (fac_bytes > 0) lease = std::make_unique<FactorPass>(dc, (size_t)fac_bytes, stream);
   float4* fac = lease ? reinterpret_cast<float4*>(lease->ptr()) : nullptr;
@@ -1138,6 +1159,8 @@ void run_chunk_load(daric_copier* c, int64_t num_layers, const char* const* name
   p.fac = fac;
   p.groups = reinterpret_cast<const GroupDev*>(up.dev() + o_groups);
   p.num_groups = (int64_t)groups.size();
+  p.work = reinterpret_cast<unsigned long long*>(up.dev() + o_work);
+  p.first_batch = first_batch;
   if (bulk) {
     if (rotate) launch_bulk_rotate(p, bg, key, dc.sm_count, stream);
     else launch_bulk_plain(p, bg, false, dc.sm_count, stream);

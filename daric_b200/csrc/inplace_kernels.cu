@@ -96,23 +96,30 @@ __device__ __forceinline__ void rotate_unit(const LayerDev& L, uint32_t stage, i
   const int hshift = __ffs(hs) - 1;
   const int ntask = base_tasks << hshift;
   const int hi_off = NEOX ? (L.rot_vecs / 2) * 16 : 0;
+  // the unit's layer and stage fields, read once into registers: every
+  // shared-memory store below is an asm statement with a memory clobber,
+  // after which a field read through L or st would be loaded again
+  const FastDiv pair_div = L.pair_div, tok_mod = L.tok_mod;
+  const uint8_t* const table = L.table;
+  const int64_t table_row = L.table_row;
+  const int half_rot = L.half_rot, row_bytes = L.row_bytes;
+  const int64_t tok0 = st.tok0, pos_a = st.pos_a, pos_b = st.pos_b;
   for (int t = tid; t < ntask; t += nthreads) {
-    const int tc = (int)fdiv((uint32_t)t, L.pair_div);  // t / P
+    const int tc = (int)fdiv((uint32_t)t, pair_div);  // t / P
     const int c = t - tc * P;
     const int hq = tc & (hs - 1);
-    const int gs = tc >> hshift;                         // g * bs + sl
-    const int g = (int)fdiv((uint32_t)gs, L.tok_mod);
+    const int gs = tc >> hshift;                       // g * bs + sl
+    const int g = (int)fdiv((uint32_t)gs, tok_mod);
     const int sl = gs - g * bs;
     const uint32_t tr = st.trange[g];
     if (st.kb[g] == nullptr || sl < (int)(tr & 0xffffu) || sl >= (int)(tr >> 16)) continue;
-    const int64_t tok = st.tok0 + (int64_t)g * bs + sl;  // segment token
+    const int64_t tok = tok0 + (int64_t)g * bs + sl;  // segment token
     float4 q[NF / 2];
-    table_factors<T, NF>(L.table, L.table_row, L.half_rot, delta, delta ? st.pos_a : st.pos_a + tok,
-                         st.pos_b + tok, c * NF, q);
+    table_factors<T, NF>(table, table_row, half_rot, delta, delta ? pos_a : pos_a + tok, pos_b + tok, c * NF, q);
     const uint32_t cbase = stage + (uint32_t)(g * kbytes + c * 16);
 #pragma unroll 2
     for (int k = hq; k < R; k += hs) {
-      const uint32_t a = cbase + (uint32_t)((sl * sl_mul + k * k_mul) * L.row_bytes);
+      const uint32_t a = cbase + (uint32_t)((sl * sl_mul + k * k_mul) * row_bytes);
       uint4 lo = lds128(a), hi;
       if (NEOX) hi = lds128(a + hi_off);
       float dv = 0.f;

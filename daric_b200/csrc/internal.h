@@ -140,7 +140,23 @@ struct PageLaunch {
   const float4* fac;         // rotary factors (factor pre-pass output)
   const struct GroupDev* groups;  // bulk pipeline unit order
   int64_t num_groups;
+  // bulk pipeline batches: CTA b's first batch is units [b * first_batch,
+  // (b + 1) * first_batch); later ones are claimed from *work, which starts
+  // at grid * first_batch (bulk_first_batch)
+  unsigned long long* work;
+  int64_t first_batch;
 };
+
+// Grid of a bulk-pipeline launch and its first batch per CTA: about half the
+// units per CTA, at most 32 (the producer warp's prefetch width).
+inline int bulk_grid(int64_t units, int sm_count, int ctas_per_sm) {
+  const int64_t ctas = (int64_t)sm_count * ctas_per_sm;
+  return (int)(units < ctas ? units : ctas);
+}
+inline int64_t bulk_first_batch(int64_t units, int grid) {
+  const int64_t f = grid > 0 ? units / (2 * (int64_t)grid) : 1;
+  return f < 1 ? 1 : (f > 32 ? 32 : f);
+}
 
 // Bulk pipeline unit order: consecutive jobs of one chunk with the same page
 // count and factor run form a group; its units go page range by page range
