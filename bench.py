@@ -733,6 +733,17 @@ def run_ours(args):
     ms_max = _max_over_ranks([ms], dist, dev)[0]
     errors = _lib.device_errors(local)
 
+    # ---- the selection alone: device time of back-to-back calls
+    preroll()
+    sev = _events(10)
+    for a, b in sev:
+        a.record(stream)
+        wl.select()
+        b.record(stream)
+    torch.cuda.synchronize()
+    sel_ms = [a.elapsed_time(b) for a, b in sev]
+    sel_avg, sel_min = _max_over_ranks([sum(sel_ms) / len(sel_ms), min(sel_ms)], dist, dev)
+
     # ---- host cost of one call with the descriptor ring free (6 steps = 12
     # of its 16 slots, enqueued after the device went idle)
     torch.cuda.synchronize()
@@ -891,6 +902,9 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (staging + paged cache >> 126 MB), no flush",
                        "selection": "second stream, beside the next step's load" if overlap else "in line"},
             "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config in (2, 4) else None,
+            "select_device_us": {"avg": round(sel_avg * 1e3, 2), "min": round(sel_min * 1e3, 2),
+                                 "note": "the selection alone, back-to-back calls (in the step it runs beside "
+                                         "the next load)"},
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
