@@ -62,6 +62,12 @@ def rope_table(max_pos, rot_dim, base, dtype):
 
 
 CONFIGS = {
+    # the reference's CPU-runnable case, one layer and one reused
+    # 512-token chunk rotated by a position delta of U[0, 4096); deviation scores from the
+    # fused load, 15% selected (a launch-bound call: its line reports us per call)
+    1: dict(name="llama3-8b-single-layer", layers=1, kv_heads=8, head_dim=128, block_size=16, theta=5e5,
+            ratio=0.15, requests=1, chunks=1, chunk_len=(512, 512), suffix=0, scores="deviation", tp=False,
+            delta=(0, 4096)),
     # one 8K prompt of 16 reused 512-token chunks (default)
     2: dict(name="llama3-8b-8k-prompt", layers=32, kv_heads=8, head_dim=128, block_size=16, theta=5e5,
             ratio=0.15, requests=1, chunks=16, chunk_len=(512, 512), suffix=0, scores="lognormal", tp=False),
@@ -127,6 +133,10 @@ class Workload:
             saved = [0] * len(lens)
             for slot, o in enumerate(order):
                 saved[o] = saved_starts[slot]
+            if "delta" in c:  # saved at the request's start, moved by a random delta
+                lo, hi = c["delta"]
+                saved = list(starts)
+                starts = [st + int(torch.randint(lo, hi, (1,), generator=g)) for st in starts]
             self.chunk_len += lens
             self.new_pos += starts
             self.old_pos += saved
@@ -765,7 +775,8 @@ def run_ours(args):
                  "note": "median host time per call with the descriptor ring free (no back-pressure)"}
 
     # ---- the unfused paths (strict PIC in place, and scatter + in-place flexible)
-    paths = time_paths(wl, dev, stream, peak, dist) if not tp else None
+    # (strict PIC rotates the middle chunks of a request: none in config 1)
+    paths = time_paths(wl, dev, stream, peak, dist) if not tp and cfg["chunks"] >= 3 else None
 
     # ---- e2e: public API from pinned host buffers; each step builds its
     # request's load plan and uploads its block ids, as a server does per
@@ -901,7 +912,7 @@ def run_ours(args):
                                       (f" (rank-0 shard of tp{shard} on one GPU)" if shard else ""),
                        "l2": "inputs larger than L2 (staging + paged cache >> 126 MB), no flush",
                        "selection": "second stream, beside the next step's load" if overlap else "in line"},
-            "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config in (2, 4) else None,
+            "us_per_prompt": round(ms_max / args.steps * 1e3, 2) if args.config in (1, 2, 4) else None,
             "select_device_us": {"avg": round(sel_avg * 1e3, 2), "min": round(sel_min * 1e3, 2),
                                  "note": "the selection alone, back-to-back calls (in the step it runs beside "
                                          "the next load)"},
@@ -1009,8 +1020,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-chunks", type=int, default=4)
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2,
-                    help="BASELINE.json config: 2 (default, 8K prompt), 3 (64-request batch), 4 (70B, TP heads), "
-                         "5 (Mistral-7B data-parallel hit/recompute sweep)")
+                    help="BASELINE.json config: 1 (one layer, one 512-token chunk), 2 (default, 8K prompt), "
+                         "3 (64-request batch), 4 (70B, TP heads), 5 (Mistral-7B data-parallel hit/recompute sweep)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--hit", type=float, default=None, help="config 5: reused share of the chunks (0.5/0.75/0.95)")
     ap.add_argument("--recompute", type=float, default=None, help="recompute ratio (top share per layer/request)")

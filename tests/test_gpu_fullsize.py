@@ -1,6 +1,8 @@
 """Full-size parity of the fused load with the CPU oracle, at the BASELINE
 shapes (bench.Workload inputs):
 
+* config 1 (one layer, one 512-token chunk moved by a random delta): every
+  page and every deviation score;
 * config 2 (32 layers x 8K tokens, 2.1 GB per load): every page of every
   layer against the oracle: K rotated by the flexible factors, V copied,
   byte for byte;
@@ -114,6 +116,19 @@ def test_config4_tp_shard_pages_and_scores_match_oracle(tp):
     wl = _workload(4, seed=0, rank=0, world=tp)
     assert wl.heads == 8 // tp
     check_against_oracle(wl, range(len(wl.chunk_len)), scores=wl.scores)
+    del wl
+    torch.cuda.empty_cache()
+
+
+def test_config1_single_layer_matches_oracle():
+    """one layer, one 512-token chunk rotated by a random
+    position delta, deviation scores written by the fused load."""
+    wl = _workload(1, seed=0)
+    assert len(wl.chunk_len) == 1 and wl.new_pos[0] != wl.old_pos[0]
+    check_against_oracle(wl, [0], scores=wl.scores)
+    sel = wl.select()
+    assert int(sel.count.cpu()[0, 0]) == int(0.15 * 512)
+    assert _lib.device_errors(0) == 0
     del wl
     torch.cuda.empty_cache()
 
