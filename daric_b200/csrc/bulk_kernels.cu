@@ -72,12 +72,6 @@ __device__ __forceinline__ int64_t find_group(const GroupDev* groups, int64_t n,
   return lo;
 }
 
-// Factor entry {C[d0], C[d0+1], S[d0], S[d0+1]} stored as 4 x bf16 (low
-// half = d0): widening bf16 to fp32 is exact.
-__device__ __forceinline__ float4 widen_factors(uint2 w) {
-  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
-                     __uint_as_float(w.y & 0xffff0000u));
-}
 __device__ __forceinline__ float4 as_float4(uint4 w) {
   return make_float4(__uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w));
 }

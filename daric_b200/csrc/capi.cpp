@@ -1492,8 +1492,16 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
       std::vector<LayerDev> ld(grp.size());
       for (size_t l = 0; l < grp.size(); ++l) ld[l] = base_layer_dev(*grp[l]);
       // the copy-engine pipeline reads the factors from the table itself
+      // (DELTA: one row per segment), or in FLEXIBLE mode from a factor
+      // pre-pass on the side stream (one combination of the two rows per
+      // token instead of one per rotation task; DARIC_INPLACE_FACTORS=table
+      // keeps the table reads for A/B measurements)
       const InplaceGeom ig = plan_inplace(dc, ld, grp[0]->tab_dtype);
       const int64_t upp = ig.nstage >= 3 ? ig.pages_per_unit : 1;
+      const char* fv = std::getenv("DARIC_INPLACE_FACTORS");
+      const bool prepass =
+          ig.nstage >= 3 && mode == DARIC_ROPE_FLEXIBLE && !(fv && std::strcmp(fv, "table") == 0);
+      const bool compact = prepass && grp[0]->tab_dtype == DARIC_DTYPE_BF16;
       std::vector<SegDev> segs;
       std::vector<FacJobDev> runs;
       segs.reserve(num_segs);
@@ -1524,7 +1532,7 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
         d.unit_begin = units;
         d.fac_tok = tok;
         units += d.num_units;
-        if (ig.nstage < 3) {
+        if (ig.nstage < 3 || prepass) {
           FacJobDev f{};
           f.table = T0.table;
           f.table_row = T0.table_row;
@@ -1562,8 +1570,27 @@ int daric_copier_rerotate_inplace(daric_copier* c, int64_t num_layers, const cha
       p.err = dc.err_word;
       const RotKey key{L0.kv_dtype, grp[0]->tab_dtype, L0.neox};
       if (ig.nstage >= 3) {
+        std::unique_ptr<FactorPass> lease;
+        if (prepass && tok > 0)
+          lease = std::make_unique<FactorPass>(dc, (size_t)tok * token_factor_bytes(T0.half_rot, compact),
+                                               (cudaStream_t)stream);
         up.send(b.size, (cudaStream_t)stream);
+        if (lease) {
+          up.also_wait(lease->stream());
+          FactorLaunch fl{};
+          fl.jobs = reinterpret_cast<const FacJobDev*>(up.dev() + o_r);
+          fl.num_jobs = (int64_t)runs.size();
+          fl.total_items = items;
+          fl.out = reinterpret_cast<float4*>(lease->ptr());
+          fl.mode = mode;
+          fl.fpv = factors_per_task(L0.kv_dtype, L0.neox != 0);
+          fl.compact = compact ? 1 : 0;
+          launch_factors(fl, grp[0]->tab_dtype, dc.sm_count, lease->stream());
+          lease->launched();
+          p.fac = reinterpret_cast<const float4*>(lease->ptr());
+        }
         launch_bulk_inplace(p, ig, key, dc.sm_count, (cudaStream_t)stream);
+        if (lease) lease->release();
         up.finish((cudaStream_t)stream);
         continue;
       }

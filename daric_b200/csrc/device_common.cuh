@@ -217,6 +217,13 @@ __device__ __forceinline__ void table_factors(const uint8_t* table, int64_t tabl
   for (int g = 0; g < NF / 2; ++g) q[g] = make_float4(oc[2 * g], oc[2 * g + 1], os[2 * g], os[2 * g + 1]);
 }
 
+// Compact factor entry {C[d0], C[d0+1], S[d0], S[d0+1]} stored as 4 x bf16
+// (low half = d0): widening bf16 to fp32 is exact.
+__device__ __forceinline__ float4 widen_factors(uint2 w) {
+  return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
+                     __uint_as_float(w.y & 0xffff0000u));
+}
+
 // Factor layout of one token (written by the factor pre-pass): the rotation
 // task c of a row (c < P = half_rot / FPV) uses FPV consecutive frequencies
 // d = c*FPV + j; they are stored as FPV/2 float4 groups

@@ -9,18 +9,22 @@
 // the page's K region (one run for token-major rows, one per head for the
 // head-major 4-D layout) into a shared-memory stage with cp.async.bulk
 // (mbarrier completion); the consumer warps rotate those rows in shared
-// memory, reading each token's cos/sin straight from the model's table
-// (DELTA: row delta; FLEXIBLE: rows old + t and new + t combined with one
-// rounding per op in the table dtype, as rope_factor), and the producer
-// writes exactly the same byte ranges back with cp.async.bulk stores. Rows of
-// other tokens of a shared page are neither loaded nor stored, so segments
-// that meet inside a page never race. V is never read.
+// memory and the producer writes exactly the same byte ranges back with
+// cp.async.bulk stores. Rows of other tokens of a shared page are neither
+// loaded nor stored, so segments that meet inside a page never race. V is
+// never read. Each token's cos/sin come from the factor buffer of the factor
+// pre-pass when the launch has one (FLEXIBLE: the pre-pass combines rows
+// old + t and new + t once per token, on a side stream beside the previous
+// kernel), else straight from the model's table (DELTA: row delta; FLEXIBLE
+// without a buffer: the two rows combined per task with one rounding per op
+// in the table dtype, as rope_factor).
 //
-// No factor pre-pass and no scratch memory. Every wait is bounded (kWaitNs):
+// Every wait is bounded (kWaitNs):
 // a wait that gives up sets DEV_ERR_TIMEOUT, the producer drains the loads
 // still in flight into its stages and the CTA returns.
 #include <map>
 #include <mutex>
+#include <type_traits>
 
 #include "bulk_common.cuh"
 #include "device_common.cuh"
@@ -39,6 +43,7 @@ struct InMeta {                 // written by the producer lane that prefetched 
   uint8_t* kb[kInMaxPages];     // K region of each page in global memory; nullptr: not copied
   int64_t tok0;                 // segment token of page 0, slot 0 (may be negative)
   int64_t pos_a, pos_b;         // the segment's positions (DELTA: pos_a = delta)
+  int64_t fac_tok;              // factor-buffer token of the segment's token 0
   int32_t layer;
   int32_t npg;                  // pages in the unit
   int32_t bytes;                // bytes loaded for the unit
@@ -77,9 +82,12 @@ __device__ __forceinline__ RunGeom run_geom(const LayerDev& L) {
 // consumer threads). Consecutive lanes take consecutive columns, so a
 // quarter warp reads one contiguous 128-byte row segment. Only tokens inside
 // the page's range are touched.
+// fac: the launch's factor buffer (compact 4 x bf16 entries for bf16
+// tables, 4 x fp32 otherwise; entry c + k * P of token t at index
+// t * half_rot / 2 + c + k * P), or nullptr to read the table.
 template <class E, class T, bool NEOX>
 __device__ __forceinline__ void rotate_unit(const LayerDev& L, uint32_t stage, int kbytes, const InMeta& st,
-                                            bool delta, int tid, int nthreads) {
+                                            bool delta, const uint8_t* fac, int tid, int nthreads) {
   constexpr int N = E::kPerVec;
   constexpr int NF = NEOX ? N : N / 2;  // frequencies of one column
   const int P = L.pair_vecs;
@@ -103,7 +111,9 @@ __device__ __forceinline__ void rotate_unit(const LayerDev& L, uint32_t stage, i
   const uint8_t* const table = L.table;
   const int64_t table_row = L.table_row;
   const int half_rot = L.half_rot, row_bytes = L.row_bytes;
-  const int64_t tok0 = st.tok0, pos_a = st.pos_a, pos_b = st.pos_b;
+  const int64_t tok0 = st.tok0, pos_a = st.pos_a, pos_b = st.pos_b, fac_tok = st.fac_tok;
+  constexpr bool kCompact = std::is_same<T, Elem<DARIC_DTYPE_BF16>>::value;
+  constexpr int ES = kCompact ? 8 : 16;  // bytes of a factor-buffer entry
   for (int t = tid; t < ntask; t += nthreads) {
     const int tc = (int)fdiv((uint32_t)t, pair_div);  // t / P
     const int c = t - tc * P;
@@ -115,7 +125,17 @@ __device__ __forceinline__ void rotate_unit(const LayerDev& L, uint32_t stage, i
     if (st.kb[g] == nullptr || sl < (int)(tr & 0xffffu) || sl >= (int)(tr >> 16)) continue;
     const int64_t tok = tok0 + (int64_t)g * bs + sl;  // segment token
     float4 q[NF / 2];
-    table_factors<T, NF>(table, table_row, half_rot, delta, delta ? pos_a : pos_a + tok, pos_b + tok, c * NF, q);
+    if (fac != nullptr) {
+      const uint8_t* fq = fac + ((fac_tok + tok) * (half_rot / 2) + c) * ES;
+#pragma unroll
+      for (int k = 0; k < NF / 2; ++k) {
+        const uint8_t* gp = fq + k * P * ES;
+        q[k] = kCompact ? widen_factors(__ldg(reinterpret_cast<const uint2*>(gp)))
+                        : __ldg(reinterpret_cast<const float4*>(gp));
+      }
+    } else {
+      table_factors<T, NF>(table, table_row, half_rot, delta, delta ? pos_a : pos_a + tok, pos_b + tok, c * NF, q);
+    }
     const uint32_t cbase = stage + (uint32_t)(g * kbytes + c * 16);
 #pragma unroll 2
     for (int k = hq; k < R; k += hs) {
@@ -193,6 +213,7 @@ __global__ void __launch_bounds__(kInThreads, 1) bulk_inplace_kernel(InplaceLaun
       mine.npg = npg;
       mine.pos_a = sg.pos_a;
       mine.pos_b = sg.pos_b;
+      mine.fac_tok = sg.fac_tok;
       mine.tok0 = (int64_t)pg0 * L.page_size - sg.tok_start;
       int bytes = 0;
       for (int q = 0; q < kInMaxPages; ++q) {
@@ -316,7 +337,8 @@ __global__ void __launch_bounds__(kInThreads, 1) bulk_inplace_kernel(InplaceLaun
     const InMeta& st = meta[s];
     if (st.bytes > 0) {
       const LayerDev& L = p.layers[st.layer];
-      rotate_unit<E, T, NEOX>(L, sbase + (uint32_t)(s * g.stage_bytes), g.kbytes, st, delta, tid, cwarps * 32);
+      rotate_unit<E, T, NEOX>(L, sbase + (uint32_t)(s * g.stage_bytes), g.kbytes, st, delta,
+                              reinterpret_cast<const uint8_t*>(p.fac), tid, cwarps * 32);
       fence_proxy_async();
     }
     __syncwarp();

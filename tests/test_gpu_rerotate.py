@@ -18,11 +18,13 @@ pytestmark = pytest.mark.gpu
 
 _TORCH = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
 
-# in-place kernel variants: the copy-engine pipeline as planned, pinned to 1
-# and 2 CTAs per SM, with 3-page units (ragged last units) and 4 consumer
-# warps, and the SIMT kernel with its factor pre-pass
+# in-place kernel variants: the copy-engine pipeline as planned (flexible
+# mode reads a factor pre-pass), with the factors read from the table per
+# task, pinned to 1 and 2 CTAs per SM, with 3-page units (ragged last units)
+# and 4 consumer warps, and the SIMT kernel with its factor pre-pass
 _INPLACE = {
     "bulk": {},
+    "bulk-table": {"DARIC_INPLACE_FACTORS": "table"},
     "bulk-1cta": {"DARIC_INPLACE_CTAS": "1"},
     "bulk-2cta": {"DARIC_INPLACE_CTAS": "2"},
     "bulk-u3-4w": {"DARIC_INPLACE_UNIT_PAGES": "3", "DARIC_INPLACE_CWARPS": "4"},
@@ -33,7 +35,8 @@ _INPLACE = {
 @pytest.fixture(params=list(_INPLACE), autouse=True)
 def inplace_kernel(request, monkeypatch):
     """Runs every test of this module with each in-place kernel."""
-    for k in ("DARIC_PAGE_KERNEL", "DARIC_INPLACE_CTAS", "DARIC_INPLACE_UNIT_PAGES", "DARIC_INPLACE_CWARPS"):
+    for k in ("DARIC_PAGE_KERNEL", "DARIC_INPLACE_CTAS", "DARIC_INPLACE_UNIT_PAGES", "DARIC_INPLACE_CWARPS",
+              "DARIC_INPLACE_FACTORS"):
         monkeypatch.delenv(k, raising=False)
     for k, v in _INPLACE[request.param].items():
         monkeypatch.setenv(k, v)
