@@ -31,7 +31,9 @@ ROPE_DELTA = 2
 SELECT_TOPK = 0
 SELECT_THRESHOLD = 1
 
-_i64p = C.POINTER(C.c_int64)
+# int64 host arrays pass as addresses (numpy's ctypes.data): building a
+# POINTER(c_int64) object per array costs more than the call's C side
+_i64p = C.c_void_p
 _i32p = C.POINTER(C.c_int32)
 _vp = C.c_void_p
 
@@ -112,10 +114,12 @@ def check(status: int) -> None:
         raise DaricError(status, msg)
 
 
-def i64(values) -> tuple[np.ndarray, C.POINTER(C.c_int64)]:
-    """int64 host array + pointer (keep the array alive while the pointer is used)."""
-    a = np.ascontiguousarray(np.asarray(values, dtype=np.int64).reshape(-1))
-    return a, a.ctypes.data_as(_i64p)
+def i64(values) -> tuple[np.ndarray, int]:
+    """int64 host array + its address (keep the array alive while the address is used)."""
+    a = values
+    if not (type(a) is np.ndarray and a.dtype == np.int64 and a.ndim == 1 and a.flags.c_contiguous):
+        a = np.ascontiguousarray(np.asarray(values, dtype=np.int64).reshape(-1))
+    return a, a.ctypes.data
 
 
 def names_array(names) -> C.Array:

@@ -111,7 +111,7 @@ def score_select(scores: torch.Tensor, block_table: torch.Tensor, block_size: in
         if out.idx.shape[1] < out_ld or out.idx.shape[0] < L or out.count.shape != (L, nseg):
             raise RuntimeError("preallocated selection output is too small")
         out.out_off = out_off
-    p64 = lambda a: a.ctypes.data_as(C.POINTER(C.c_int64))
+    p64 = lambda a: a.ctypes.data
     s = stream or torch.cuda.current_stream(dev).cuda_stream
     check(_lib.load().daric_score_select(
         C.c_void_p(scores.data_ptr()), L, scores.stride(0), nseg, p64(cols), p64(lens), p64(pos0), p64(kk),
