@@ -16,6 +16,21 @@ def declared_symbols():
     return sorted(set(re.findall(r"DARIC_API\s+[\w\s\*]+?\b(daric_\w+)\s*\(", text)))
 
 
+def test_i64_passes_int64_arrays_by_address():
+    """Host int64 arrays reach the C ABI as addresses: a contiguous int64
+    vector is used as is, anything else is converted to one first."""
+    import numpy as np
+    a = np.arange(5, dtype=np.int64)
+    arr, addr = _lib.i64(a)
+    assert arr is a and addr == a.ctypes.data
+    for src in ([3, 1, 2], np.arange(6, dtype=np.int64)[::2], np.arange(3, dtype=np.int32), np.ones((2, 2), np.int64)):
+        arr, addr = _lib.i64(src)
+        assert arr.dtype == np.int64 and arr.ndim == 1 and arr.flags.c_contiguous
+        assert addr == arr.ctypes.data
+        np.testing.assert_array_equal(arr, np.asarray(src).reshape(-1))
+        assert np.ctypeslib.as_array((C.c_int64 * arr.size).from_address(addr)).tolist() == arr.tolist()
+
+
 def test_header_declares_entry_points():
     syms = declared_symbols()
     assert "daric_copier_scatter_pages" in syms and "daric_score_select" in syms
