@@ -142,11 +142,20 @@ __device__ __forceinline__ void rotate_unit_smem(const LayerDev& L, uint8_t* sta
             q[k] = FC ? widen_factors(lds64(ad)) : as_float4(lds128(ad));
           }
         } else {
+          // factors in L2, contiguous per task: the task's NG entries start
+          // at entry c * NG of the token (16-byte aligned: NG * ES is a
+          // multiple of 16 for every element type)
+          const uint8_t* tq = fac_unit + (gs * per_tok + c * NG) * ES;
+          if constexpr (FC) {
 #pragma unroll
-          for (int k = 0; k < NG; ++k) {
-            const uint8_t* gp = fq + k * P * ES;
-            q[k] = FC ? widen_factors(__ldg(reinterpret_cast<const uint2*>(gp)))
-                      : __ldg(reinterpret_cast<const float4*>(gp));
+            for (int k = 0; k < NG; k += 2) {
+              const uint4 w = __ldg(reinterpret_cast<const uint4*>(tq + k * ES));
+              q[k] = widen_factors(make_uint2(w.x, w.y));
+              q[k + 1] = widen_factors(make_uint2(w.z, w.w));
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < NG; ++k) q[k] = __ldg(reinterpret_cast<const float4*>(tq + k * ES));
           }
         }
         const uint32_t cb = base + (uint32_t)(g * rbytes + c * 16);

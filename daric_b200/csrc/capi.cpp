@@ -899,6 +899,7 @@ void run_page_jobs(daric_copier* c, const JobPlan& jp, const std::vector<int64_t
     fl.mode = mode;
     fl.fpv = factors_per_task(key.kv_dtype, key.neox != 0);
     fl.compact = compact ? 1 : 0;
+    fl.contig = (bg.nstage >= 3 && !bg.fac_off) ? 1 : 0;  // the bulk kernel reads factors from L2
     launch_factors(fl, key.tab_dtype, dc.sm_count, lease->stream());
   }
   if (lease) lease->launched();
@@ -1139,6 +1140,7 @@ void run_chunk_load(daric_copier* c, int64_t num_layers, const char* const* name
     fl.mode = mode;
     fl.fpv = factors_per_task(key.kv_dtype, key.neox != 0);
     fl.compact = compact ? 1 : 0;
+    fl.contig = (bg.nstage >= 3 && !bg.fac_off) ? 1 : 0;  // the bulk kernel reads factors from L2
     launch_factors(fl, key.tab_dtype, dc.sm_count, lease->stream());
   }
   if (lease) lease->launched();

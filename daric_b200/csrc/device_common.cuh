@@ -229,7 +229,10 @@ __device__ __forceinline__ float4 widen_factors(uint2 w) {
 // d = c*FPV + j; they are stored as FPV/2 float4 groups
 //   q[g*P + c] = {C[d0], C[d0+1], S[d0], S[d0+1]},  d0 = c*FPV + 2g,
 // so the 32 lanes of a warp (consecutive c) read consecutive 16-byte words.
-// FPV = elements per 16-byte vector (NeoX) or half of it (GPT-J).
+// FPV = elements per 16-byte vector (NeoX) or half of it (GPT-J). Launches
+// that read the factors from L2 instead of shared memory use the contiguous
+// form q[c*NG + g] (NG = FPV/2 entries of a task in one run: one or a few
+// 16-byte loads per task).
 
 // x1' = x1*C - x2*S ; x2' = x2*C + x1*S on NeoX halves, in fp32 with every
 // product and sum rounded separately (__fmul_rn / __fadd_rn / __fsub_rn are

@@ -242,7 +242,7 @@ struct FactorLaunch {
   int32_t mode;
   int32_t fpv;          // factors per rotation task
   int32_t compact;      // entries are 4 x bf16 (8 bytes) instead of 4 x fp32
-  int32_t pad;
+  int32_t contig;       // a task's entries are contiguous (c * NG + g) instead of strided (g * P + c)
 };
 
 // Factor bytes of one token (half_rot (cos, sin) pairs): fp32, or bf16 when

@@ -125,7 +125,9 @@ __global__ void __launch_bounds__(256) factor_kernel(FactorLaunch p) {
     if (p.mode == DARIC_ROPE_FLEXIBLE) { a += t; b += t; }
     const float2 f0 = rope_factor<T>(jb.table, jb.table_row, jb.half_rot, p.mode, a, b, d0);
     const float2 f1 = rope_factor<T>(jb.table, jb.table_row, jb.half_rot, p.mode, a, b, d0 + 1);
-    const int64_t e = (jb.out_tok + t) * per_tok + k;
+    // entry (g, c): strided g * P + c (consecutive lanes read consecutive
+    // words), or contiguous c * NG + g (a task's NG entries in one run)
+    const int64_t e = (jb.out_tok + t) * per_tok + (p.contig ? c * (per_tok / jb.P) + g : k);
     if (p.compact) {
       // bf16 table: every factor is already a bf16 value (rounded in
       // rope_factor), so its upper 16 bits are the exact bf16 encoding
